@@ -1,0 +1,437 @@
+"""Benchmark of the B200 GGML quantized matmul (BASELINE.json metric:
+"Q4_K GEMM TFLOP/s (M=256) & GEMV weight-GB/s (M=1), % of roofline, 1/2/4/8 GPU").
+
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
+    python -m torch.distributed.run --nproc-per-node N --master-addr 127.0.0.1 bench.py --gpus N
+
+Workload (config.workload "q4k_ffn_up_m256"): BASELINE config 1's projection (Q4_K weights,
+K=2560 -> N=10240, 256-element super-blocks with the config's value distributions) at M=256 bf16
+activation rows -- the size the metric is quoted at. One step is one pass over a stack of
+L=36 distinct weight matrices (36 x 14.7 MB = 531 MB of weights, > 4x the 126 MB L2, so every
+matrix streams from HBM), each product writing its own f32 output. Synthetic seeded data.
+
+With N GPUs (one process per GPU, NCCL): the projection is column-sharded -- every rank owns a
+10240-column shard of an N*10240-wide layer (per-GPU work fixed: weak scaling) -- and each
+layer's f32 output shard is all-gathered over NVLink (torch.distributed / NCCL) on a second
+stream, overlapped with the next layer's product.
+
+Printed JSON (rank 0): `value` = aggregate TFLOP/s of the timed steps (inputs resident in HBM,
+device-timed with CUDA events, max over ranks); `e2e` = the same through the public API with
+pinned host buffers (per step: activations host->device, the layer stack, the last layer's output
+device->host); `roofline` = the tensor-core kernel's achieved TFLOP/s per launch vs the measured
+bf16 peak; `gemv` = the M=1 weight-streaming GB/s on the same matrices; `cpu_baseline` = the
+reference's CPU arithmetic (quant.rs dequant restated in C + a CPU f32 matmul) on a bounded sample.
+"""
+from __future__ import annotations
+
+import argparse
+import json
+import os
+import statistics
+import sys
+import threading
+import time
+
+REPO = os.path.dirname(os.path.abspath(__file__))
+for p in (os.path.join(REPO, "jevons-rs_b200"), REPO):
+    if p not in sys.path:
+        sys.path.insert(0, p)
+
+import numpy as np  # noqa: E402
+
+K_DIM, N_DIM, M_ROWS, LAYERS = 2560, 10240, 256, 36
+METRIC = "Q4_K GEMM TFLOP/s (M=256)"
+WORKLOAD = "q4k_ffn_up_m256"
+Q4_K = 12
+FALLBACK_PEAKS = {"hbm_gbs": 6650.0, "bf16_tflops": 1590.0, "bf16_tflops_sustained": 1400.0}
+
+
+def peaks():
+    path = os.path.join(REPO, "MEASURED_PEAKS.json")
+    try:
+        with open(path) as f:
+            d = json.load(f)
+        return d, "measured"
+    except Exception:
+        return dict(FALLBACK_PEAKS), "fallback"
+
+
+# ------------------------------------------------------------------------------------------------
+# clocks during the timed region (NVML, the library nvidia-smi reads)
+# ------------------------------------------------------------------------------------------------
+class ClockSampler:
+    REASONS = {  # nvmlClocksEventReason bits
+        0x1: "gpu_idle", 0x2: "applications_clocks_setting", 0x4: "sw_power_cap", 0x8: "hw_slowdown",
+        0x10: "sync_boost", 0x20: "sw_thermal_slowdown", 0x40: "hw_thermal_slowdown", 0x80: "hw_power_brake_slowdown",
+        0x100: "display_clock_setting",
+    }
+
+    def __init__(self, torch_device: int):
+        self.samples, self.reasons, self.max_mhz = [], set(), None
+        self._stop = threading.Event()
+        self._ok = False
+        try:
+            import pynvml as nv
+            nv.nvmlInit()
+            self.nv = nv
+            import torch
+            uuid = str(torch.cuda.get_device_properties(torch_device).uuid)
+            uuid = uuid if uuid.startswith("GPU-") else "GPU-" + uuid
+            try:
+                self.h = nv.nvmlDeviceGetHandleByUUID(uuid.encode() if isinstance(uuid, str) else uuid)
+            except Exception:
+                self.h = nv.nvmlDeviceGetHandleByIndex(torch_device)
+            self.max_mhz = nv.nvmlDeviceGetMaxClockInfo(self.h, nv.NVML_CLOCK_SM)
+            self._ok = True
+        except Exception as e:  # NVML missing: report that instead of clocks
+            self.err = repr(e)
+
+    def _run(self):
+        nv = self.nv
+        while not self._stop.is_set():
+            try:
+                self.samples.append(nv.nvmlDeviceGetClockInfo(self.h, nv.NVML_CLOCK_SM))
+                try:
+                    bits = nv.nvmlDeviceGetCurrentClocksEventReasons(self.h)
+                except AttributeError:
+                    bits = nv.nvmlDeviceGetCurrentClocksThrottleReasons(self.h)
+                for b, name in self.REASONS.items():
+                    if bits & b and name != "gpu_idle":
+                        self.reasons.add(name)
+            except Exception:
+                pass
+            time.sleep(0.01)
+
+    def __enter__(self):
+        if self._ok:
+            self._t = threading.Thread(target=self._run, daemon=True)
+            self._t.start()
+        return self
+
+    def __exit__(self, *a):
+        if self._ok:
+            self._stop.set()
+            self._t.join()
+
+    def report(self):
+        if not self._ok:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": [], "error": getattr(self, "err", "nvml")}
+        return {"sm_mhz": statistics.median(self.samples) if self.samples else None, "sm_max_mhz": self.max_mhz,
+                "reasons": sorted(self.reasons), "samples": len(self.samples)}
+
+
+# ------------------------------------------------------------------------------------------------
+# CPU baseline: the reference's block dequant (restated in C, oracle/) + CPU f32 matmul
+# ------------------------------------------------------------------------------------------------
+def cpu_gemm_sample(raw: np.ndarray, x_f32: np.ndarray, n_cols: int):
+    """Dequantizes the first n_cols weight rows (oracle) and multiplies with torch's CPU f32 matmul.
+    Returns (seconds total, seconds of dequant)."""
+    import torch
+    from oracle import oracle
+    row_bytes = K_DIM // 256 * 144
+    t0 = time.perf_counter()
+    w = oracle.dequantize(Q4_K, raw[: n_cols * row_bytes]).reshape(n_cols, K_DIM)
+    t1 = time.perf_counter()
+    out = torch.from_numpy(x_f32) @ torch.from_numpy(w).t()
+    t2 = time.perf_counter()
+    del out
+    return t2 - t0, t1 - t0
+
+
+def cpu_baseline(raw: np.ndarray, x_f32: np.ndarray, budget_s: float = 12.0):
+    import torch
+    threads = os.cpu_count() or 1
+    torch.set_num_threads(threads)
+    n_cols = 2048
+    cpu_gemm_sample(raw, x_f32, 256)  # warm-up (thread pools, page faults)
+    runs, total, deq = 0, 0.0, 0.0
+    t_start = time.perf_counter()
+    while time.perf_counter() - t_start < budget_s or runs < 3:
+        a, b = cpu_gemm_sample(raw, x_f32, n_cols)
+        total += a
+        deq += b
+        runs += 1
+    flops = 2.0 * M_ROWS * n_cols * K_DIM * runs
+    return {
+        "value": flops / total / 1e12, "unit": "TFLOP/s", "cores": threads, "kind": "port",
+        "sample": f"{runs} x Q4_K [M={M_ROWS}, K={K_DIM}] x [{n_cols} of the {N_DIM} weight rows]: oracle dequant "
+                  f"(quant.rs restated in C, OpenMP) + torch CPU f32 matmul; dequant share "
+                  f"{deq / total:.0%}, without dequant {flops / max(total - deq, 1e-9) / 1e12:.3f} TFLOP/s",
+        "cpu": _cpu_model(),
+    }
+
+
+def _cpu_model():
+    try:
+        for line in open("/proc/cpuinfo"):
+            if line.startswith("model name"):
+                return line.split(":", 1)[1].strip()
+    except Exception:
+        pass
+    return "unknown"
+
+
+def run_reference(args):
+    """--impl reference: the reference's CPU arithmetic for this path on the host cores.
+
+    The reference (Rust / CubeCL / HIP) cannot be built here (no cargo/rustc, no network) and its
+    kernels have no CPU implementation, so this arm times the restatement of its block dequant
+    (oracle/jk_oracle.c, quant.rs:25-101) feeding a CPU f32 matmul -- the stand-in named in the
+    baseline plan. Each step is a bounded sample of the same workload (2048 of the 10240 weight rows)."""
+    rank = int(os.environ.get("RANK", "0"))
+    if rank != 0:
+        return 0
+    import torch
+    from jevons_kernels import synth
+    threads = os.cpu_count() or 1
+    torch.set_num_threads(threads)
+    rng = np.random.default_rng(1)
+    raw = synth.q4k_blocks(rng, N_DIM, K_DIM)
+    x = synth.activations(np.random.default_rng(2), M_ROWS, K_DIM, round_to="bf16")
+    n_cols = 2048
+    for _ in range(max(args.warmup, 1)):
+        cpu_gemm_sample(raw, x, n_cols)
+    times = []
+    for _ in range(args.steps):
+        a, _ = cpu_gemm_sample(raw, x, n_cols)
+        times.append(a)
+    total = sum(times)
+    value = 2.0 * M_ROWS * n_cols * K_DIM * len(times) / total / 1e12
+    line = {
+        "impl": "reference", "metric": METRIC, "value": value, "unit": "TFLOP/s", "n_gpus": args.gpus,
+        "steps": args.steps, "warmup": args.warmup, "ms_per_step": 1e3 * total / len(times),
+        "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "f32", "data": "synthetic",
+        "config": {"workload": WORKLOAD, "m": M_ROWS, "k": K_DIM, "n": N_DIM, "weights": "Q4_K",
+                   "sample_weight_rows": n_cols},
+        "cpu_baseline": {"value": value, "unit": "TFLOP/s", "cores": threads, "kind": "port",
+                         "sample": f"Q4_K [M={M_ROWS}, K={K_DIM}] x [{n_cols} weight rows] per step: oracle dequant "
+                                   "(quant.rs restated in C) + torch CPU f32 matmul", "cpu": _cpu_model()},
+        "e2e": {"value": value, "unit": "TFLOP/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
+    }
+    print(json.dumps(line), flush=True)
+    return 0
+
+
+# ------------------------------------------------------------------------------------------------
+# our arm
+# ------------------------------------------------------------------------------------------------
+def run_ours(args):
+    import torch
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    torch.cuda.set_device(local)
+    dist = None
+    if world > 1:
+        import datetime
+        import torch.distributed as dist
+        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=120), device_id=torch.device("cuda", local))
+
+    from jevons_kernels import synth
+    from jevons_kernels.gemm import Buf, Gpu, Plan, QMatrix, SplitScratch, matmul, matvec
+
+    gpu = Gpu(local)
+    dev = torch.device("cuda", local)
+    L = args.layers
+    rng = np.random.default_rng(1 + 1000 * rank)
+    raw = synth.q4k_blocks(rng, N_DIM, K_DIM)  # this rank's 10240-column shard
+    # L distinct device copies (distinct memory defeats L2 reuse across the stack)
+    ws = [QMatrix.upload(gpu, Q4_K, N_DIM, K_DIM, 1, raw) for _ in range(L)]
+    x = torch.from_numpy(synth.activations(np.random.default_rng(2), M_ROWS, K_DIM)).to(dev).bfloat16()
+    outs = [torch.empty(M_ROWS, N_DIM, device=dev) for _ in range(L)]
+    scratch = SplitScratch(gpu)
+    plan = Plan.heuristic(ws[0], M_ROWS, False)
+    launches_per_product = 1 + (1 if plan.splits > 1 else 0)
+    xb = Buf(x)
+    obufs = [Buf(o) for o in outs]
+
+    comm_stream = torch.cuda.Stream(device=dev) if world > 1 else None
+    gathered = [torch.empty(world, M_ROWS, N_DIM, device=dev) for _ in range(L)] if world > 1 else None
+
+    def step(xbuf=xb):
+        cur = torch.cuda.current_stream()
+        for i in range(L):
+            matmul(gpu, xbuf, M_ROWS, ws[i], obufs[i], None, scratch)
+            if world > 1:
+                ev = torch.cuda.Event()
+                ev.record(cur)
+                comm_stream.wait_event(ev)
+                with torch.cuda.stream(comm_stream):
+                    dist.all_gather_into_tensor(gathered[i], outs[i])
+        if world > 1:
+            ev = torch.cuda.Event()
+            ev.record(comm_stream)
+            cur.wait_event(ev)
+
+    def barrier():
+        torch.cuda.synchronize()
+        if dist is not None:
+            dist.barrier()
+        torch.cuda.synchronize()
+
+    def max_over_ranks(v: float) -> float:
+        if dist is None:
+            return v
+        t = torch.tensor([v], device=dev, dtype=torch.float64)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        return float(t.item())
+
+    flops_step = 2.0 * M_ROWS * N_DIM * K_DIM * L  # per rank
+
+    # ---- value: device-resident inputs --------------------------------------------------------
+    for _ in range(args.warmup):
+        step()
+    barrier()
+    sampler = ClockSampler(local)
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    with sampler:
+        e0.record()
+        for _ in range(args.steps):
+            step()
+        e1.record()
+        torch.cuda.synchronize()
+    ms = max_over_ranks(e0.elapsed_time(e1))
+    value = flops_step * world * args.steps / (ms * 1e-3) / 1e12
+
+    # ---- roofline: average duration of one product launch (gemm [+ split reduce]) -------------
+    reps = 3
+    evs = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)) for _ in range(L * reps)]
+    barrier()
+    for r in range(reps):
+        for i in range(L):
+            a, b = evs[r * L + i]
+            a.record()
+            matmul(gpu, xb, M_ROWS, ws[i], obufs[i], None, scratch)
+            b.record()
+    torch.cuda.synchronize()
+    per_launch_ms = statistics.mean(a.elapsed_time(b) for a, b in evs)
+    pk, pk_kind = peaks()
+    peak = pk.get("bf16_tflops_sustained", pk.get("bf16_tflops"))
+    achieved = 2.0 * M_ROWS * N_DIM * K_DIM / (per_launch_ms * 1e-3) / 1e12
+    traffic = None
+    try:
+        with open(os.path.join(REPO, "profiles", "roofline_traffic.json")) as f:
+            traffic = json.load(f).get("q4k_gemm_m256_bytes_per_launch")
+    except Exception:
+        pass
+
+    # ---- GEMV M=1 weight streaming on the same stack ------------------------------------------
+    x1 = torch.from_numpy(synth.activations(np.random.default_rng(3), 1, K_DIM)).to(dev).bfloat16()
+    o1 = [torch.empty(1, N_DIM, device=dev) for _ in range(L)]
+    x1b, o1b = Buf(x1), [Buf(o) for o in o1]
+    for _ in range(3):
+        for i in range(L):
+            matvec(gpu, x1b, 1, ws[i], o1b[i])
+    barrier()
+    gv_steps = max(args.steps, 20)
+    g0, g1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    g0.record()
+    for _ in range(gv_steps):
+        for i in range(L):
+            matvec(gpu, x1b, 1, ws[i], o1b[i])
+    g1.record()
+    torch.cuda.synchronize()
+    gv_ms = max_over_ranks(g0.elapsed_time(g1))
+    wbytes = N_DIM * K_DIM // 256 * 144
+    gemv_gbs = wbytes * L * gv_steps * world / (gv_ms * 1e-3) / 1e9
+    alg_bytes = wbytes + K_DIM * 2 + N_DIM * 4
+
+    # ---- config 1 proper (M=32) ------------------------------------------------------------
+    x32 = torch.from_numpy(synth.activations(np.random.default_rng(4), 32, K_DIM)).to(dev).bfloat16()
+    o32 = [torch.empty(32, N_DIM, device=dev) for _ in range(L)]
+    x32b, o32b = Buf(x32), [Buf(o) for o in o32]
+    for _ in range(3):
+        for i in range(L):
+            matmul(gpu, x32b, 32, ws[i], o32b[i], None, scratch)
+    barrier()
+    c0, c1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    c0.record()
+    for _ in range(gv_steps):
+        for i in range(L):
+            matmul(gpu, x32b, 32, ws[i], o32b[i], None, scratch)
+    c1.record()
+    torch.cuda.synchronize()
+    c_ms = max_over_ranks(c0.elapsed_time(c1))
+    m32_tflops = 2.0 * 32 * N_DIM * K_DIM * L * gv_steps * world / (c_ms * 1e-3) / 1e12
+
+    # ---- e2e: host buffers through the public API -------------------------------------------
+    xh = x.cpu().pin_memory()
+    oh = torch.empty(M_ROWS, N_DIM, dtype=torch.float32).pin_memory()
+    xd = torch.empty_like(x)
+    xdb = Buf(xd)
+
+    def e2e_step():
+        xd.copy_(xh, non_blocking=True)
+        step(xdb)
+        oh.copy_(outs[L - 1], non_blocking=True)
+
+    for _ in range(args.warmup):
+        e2e_step()
+    barrier()
+    h0, h1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    h0.record()
+    for _ in range(args.steps):
+        e2e_step()
+    h1.record()
+    torch.cuda.synchronize()
+    e_ms = max_over_ranks(h0.elapsed_time(h1))
+    e2e_value = flops_step * world * args.steps / (e_ms * 1e-3) / 1e12
+
+    cpu = None
+    if rank == 0 and world == 1 and not args.no_cpu_baseline:
+        x_f32 = x.float().cpu().numpy()
+        cpu = cpu_baseline(raw, x_f32)
+
+    if dist is not None:
+        dist.barrier()
+    if rank == 0:
+        line = {
+            "metric": METRIC, "value": value, "unit": "TFLOP/s", "n_gpus": world, "steps": args.steps,
+            "warmup": args.warmup, "ms_per_step": ms / args.steps, "higher_is_better": True, "scaling": "weak",
+            "vs_baseline": None, "dtype": "bf16", "data": "synthetic",
+            "config": {"workload": WORKLOAD, "weights": "Q4_K", "m": M_ROWS, "k": K_DIM, "n_per_gpu": N_DIM,
+                       "n_total": N_DIM * world, "layers_per_step": L, "plan": repr(plan),
+                       "l2": "inputs larger than L2: 36 distinct weight matrices (531 MB) per step",
+                       "parallelism": f"column-shard x{world}" + (" + NCCL all-gather of f32 outputs" if world > 1 else ""),
+                       "activations": "bf16 N(0,1)"},
+            "roofline": {"bound": "tensor", "achieved": achieved, "peak": peak, "unit": "TFLOP/s",
+                         "frac": achieved / peak, "traffic": traffic,
+                         "kernel": "gemm_tc_kernel<Q4_K,bf16,256> (+ reduce_splits when split-K)",
+                         "per_launch_ms": per_launch_ms,
+                         "peak_source": f"{pk_kind} bf16_tflops_sustained (kernel timed inside a long step)"},
+            "gemv": {"metric": "Q4_K GEMV weight-GB/s (M=1)", "value": gemv_gbs, "unit": "GB/s",
+                     "peak_hbm_gbs": pk.get("hbm_gbs"), "frac_of_hbm": gemv_gbs / pk.get("hbm_gbs", 1.0),
+                     "algorithmic_gbs": gemv_gbs * alg_bytes / wbytes, "ms_per_product": gv_ms / gv_steps / L},
+            "m32": {"metric": "Q4_K GEMM TFLOP/s (M=32, BASELINE config 1)", "value": m32_tflops, "unit": "TFLOP/s",
+                    "weight_gbs": wbytes * L * gv_steps * world / (c_ms * 1e-3) / 1e9},
+            "e2e": {"value": e2e_value, "unit": "TFLOP/s", "h2d_bytes_per_step": xh.numel() * 2,
+                    "d2h_bytes_per_step": oh.numel() * 4},
+            "gpu_launches": args.steps * L * launches_per_product,
+            "clocks": sampler.report(),
+            "cpu_baseline": cpu,
+        }
+        print(json.dumps(line), flush=True)
+    if dist is not None:
+        dist.barrier()
+        dist.destroy_process_group()
+    return 0
+
+
+def main():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=200)
+    ap.add_argument("--warmup", type=int, default=5)
+    ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
+    ap.add_argument("--layers", type=int, default=LAYERS)
+    ap.add_argument("--no-cpu-baseline", action="store_true")
+    args = ap.parse_args()
+    if args.warmup < 3:
+        args.warmup = 3
+    if args.impl == "reference":
+        return run_reference(args)
+    return run_ours(args)
+
+
+if __name__ == "__main__":
+    sys.exit(main())

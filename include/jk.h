@@ -1,0 +1,197 @@
+/*
+ * jk.h -- C ABI of the B200 (sm_100a) GGML quantized matmul.
+ *
+ * This is the drop-in boundary for the quantized matmul path of zojeda/jevons-rs: the GGML
+ * block types of `jevons-formats` and the matmul entry points of `jevons-kernels` and
+ * `jevons-burn`. Each declaration names the reference item it replaces (paths are within the
+ * reference project). Only plain pointers, sizes and integer codes cross this boundary.
+ *
+ * Conventions (mirroring the reference):
+ *   - Weights W are [experts * n, k] in GGML order: row c holds output column c, and k is the
+ *     contiguous row length (crates/jevons-formats/src/gguf.rs:148-156).
+ *   - Activations x are row-major [m, k]; outputs are row-major f32 [m, n]:
+ *       out[r, c] = sum_j x[r, j] * W[c, j]       (crates/jevons-kernels/src/gemm.rs:1)
+ *   - Device pointers (x, out, scratch) are caller-owned, as the reference's `Buf`s are.
+ *   - Launches are asynchronous on `stream` (a cudaStream_t; NULL = legacy default stream);
+ *     nothing here synchronises except jk_qmatrix_* creation, jk_gpu_sync and jk_device_error.
+ *   - Every function returns a jk_status. On failure jk_last_error() returns a thread-local
+ *     message naming the tensor type and shape, like the reference's `Err(String)` values and
+ *     launcher assertions (gemm.rs:840-886, 1137, 1218). Nothing aborts or throws across the ABI.
+ */
+#ifndef JK_H
+#define JK_H
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+#define JK_ABI_VERSION 1
+
+typedef enum jk_status {
+    JK_OK = 0,
+    JK_ERR_INVALID = 1,     /* null pointer, bad enum value, buffer too small */
+    JK_ERR_UNSUPPORTED = 2, /* tensor type without a GPU layout, device not sm_100 */
+    JK_ERR_SHAPE = 3,       /* n, k, experts or byte counts that do not fit the type */
+    JK_ERR_CUDA = 4,        /* a CUDA runtime call failed (message carries cudaGetErrorString) */
+    JK_ERR_NCCL = 5,        /* an NCCL call failed */
+    JK_ERR_TIMEOUT = 6,     /* a bounded device-side wait ran out (see jk_device_error) */
+} jk_status;
+
+/* GGML type ids, as TensorType::from_id (crates/jevons-formats/src/gguf.rs:110-132). */
+typedef enum jk_tensor_type {
+    JK_TYPE_F32 = 0,
+    JK_TYPE_F16 = 1,
+    JK_TYPE_Q5_0 = 6,
+    JK_TYPE_Q8_0 = 8,
+    JK_TYPE_Q4_K = 12,
+    JK_TYPE_Q6_K = 14,
+} jk_tensor_type;
+
+/* Activation element types accepted by the matmul entry points. The reference takes FP16 only
+ * (gemm.rs:3); bf16 and f32 are additions for the B200 path. */
+typedef enum jk_dtype {
+    JK_DTYPE_F32 = 0,
+    JK_DTYPE_F16 = 1,
+    JK_DTYPE_BF16 = 2,
+} jk_dtype;
+
+/* ---- errors / library ------------------------------------------------------------------ */
+
+/* Thread-local message of the last failing call on this thread ("" if none). */
+const char *jk_last_error(void);
+int jk_abi_version(void);
+
+/* ---- block formats (host) ---------------------------------------------------------------- */
+
+/* TensorType::block (gguf.rs:134-145): elements and bytes per block. JK_ERR_UNSUPPORTED for an
+ * unknown id. */
+jk_status jk_tensor_type_block(int type, uint64_t *elements, uint64_t *bytes);
+
+/* quant::q4k_scale_min (crates/jevons-formats/src/quant.rs:14-23): 6-bit (scale, min) pair j
+ * (0..8) from the 12 packed scale bytes of a Q4_K super-block. */
+jk_status jk_q4k_scale_min(int j, const uint8_t scales[12], uint8_t *scale, uint8_t *min);
+
+/* quant::packed_words (quant.rs:128-136): words per block of the reference's SoA regions
+ * (q, h, s, d). All zero for types without a GPU layout. */
+jk_status jk_packed_words(int type, size_t words[4]);
+
+/* quant::pack (quant.rs:156-193): repacks raw GGML blocks into the reference's SoA regions.
+ * Region capacities are checked against blocks * jk_packed_words; d is f32. Pass NULL for an
+ * empty region. */
+jk_status jk_pack(int type, const void *ggml_bytes, size_t len,
+                  uint32_t *q, size_t q_words, uint32_t *h, size_t h_words,
+                  uint32_t *s, size_t s_words, float *d, size_t d_words);
+
+/* ---- device ------------------------------------------------------------------------------- */
+
+/* Gpu::new (crates/jevons-kernels/src/lib.rs:181-191): checks that `device` exists and is a
+ * Blackwell sm_100 part, and makes it current on this thread. */
+jk_status jk_gpu_init(int device);
+
+/* Gpu::sync (lib.rs:300-302): waits for all work queued on `stream`. */
+jk_status jk_gpu_sync(void *stream);
+
+/* Reads and clears the device-side error word of `device` (bounded waits that ran out record
+ * a code there instead of hanging). Synchronises the device. *code = 0 when clean. */
+jk_status jk_device_error(int device, uint32_t *code);
+
+/* ---- quantized weight matrices -------------------------------------------------------------- */
+
+typedef struct jk_qmatrix jk_qmatrix;
+
+/* QMatrix::upload (gemm.rs:832-854): validates and repacks raw GGML bytes of a
+ * [experts * n, k] matrix into the B200 layout and copies them to `device`.
+ * Errors: JK_ERR_SHAPE "<type> [<experts>x<n>, <k>] has the wrong byte count" /
+ * "... has an unsupported shape" (n % 64, k % 64, k % block), JK_ERR_UNSUPPORTED for types
+ * without a GPU layout. */
+jk_status jk_qmatrix_upload(int device, int type, size_t n, size_t k, size_t experts,
+                            const void *ggml_bytes, size_t len, jk_qmatrix **out);
+
+/* QMatrix::from_packed (gemm.rs:856-899): same, from the reference's SoA regions (jk_pack). */
+jk_status jk_qmatrix_from_packed(int device, int type, size_t n, size_t k, size_t experts,
+                                 const uint32_t *q, size_t q_words, const uint32_t *h, size_t h_words,
+                                 const uint32_t *s, size_t s_words, const float *d, size_t d_words,
+                                 jk_qmatrix **out);
+
+/* QMatrix::f16_view / from_f16_words (gemm.rs:906-948): views caller-owned row-major FP16
+ * weights [n, k] on `device` without copying (n % 64, k % 64). The view never frees them. */
+jk_status jk_qmatrix_f16_view(int device, size_t n, size_t k, const void *f16_weights_dev,
+                              jk_qmatrix **out);
+
+/* Frees a matrix (no-op for NULL). Frees device memory only if the matrix owns it. */
+void jk_qmatrix_destroy(jk_qmatrix *w);
+
+/* Fields of QMatrix (gemm.rs:818-829) and QMatrix::bytes (:950-952): the device bytes held. */
+jk_status jk_qmatrix_info(const jk_qmatrix *w, int *type, size_t *n, size_t *k, size_t *experts,
+                          size_t *device_bytes);
+
+/* Device dequantization of the whole matrix to f32 [experts * n, k], using the same decode
+ * routines as the matmul kernels. Bit-exact with quant::dequantize (quant.rs:83-101). */
+jk_status jk_qmatrix_dequantize(const jk_qmatrix *w, float *out_dev, size_t out_len, void *stream);
+
+/* ---- launch plans ---------------------------------------------------------------------------- */
+
+/* Plan (gemm.rs:973-1016). bm == 0 selects the small-row kernel (m <= JK_GEMV_ROWS).
+ * Otherwise bm is the activation-row tile of the tensor-core kernel (MMA N: 32, 64, 128 or
+ * 256), bn the weight-row tile (MMA M: 128) and splits the split-K factor (1..16). Plans with
+ * bm > 0 and splits == 1 are row invariant: every output row is accumulated in the same order
+ * whatever m or bm is (gemm.rs:1090-1091). */
+typedef struct jk_plan {
+    int32_t bm;
+    int32_t bn;
+    int32_t splits;
+} jk_plan;
+
+#define JK_GEMV_ROWS 16 /* GEMV_ROWS (gemm.rs:1019) */
+
+/* Plan::heuristic (gemm.rs:989-1004); `sms` is the multiprocessor count to fill (the
+ * reference's groups_target; 0 = the device's own count). */
+jk_status jk_plan_heuristic(const jk_qmatrix *w, size_t m, int row_invariant, int sms, jk_plan *out);
+
+/* Plan::valid_for (gemm.rs:1006-1015): 1 if `plan` can run `w` at `m` rows, else 0. */
+int jk_plan_valid_for(const jk_plan *plan, const jk_qmatrix *w, size_t m);
+
+/* ---- split-K scratch ------------------------------------------------------------------------ */
+
+/* SplitScratch (gemm.rs:1040-1065): device scratch for split-K partial sums and activation
+ * conversion, grown on demand with cudaMalloc (the growth synchronises the device). One
+ * scratch must not be used by two launches that may run at the same time. */
+typedef struct jk_split_scratch jk_split_scratch;
+jk_status jk_split_scratch_create(int device, jk_split_scratch **out);
+void jk_split_scratch_destroy(jk_split_scratch *s);
+
+/* ---- products -------------------------------------------------------------------------------- */
+
+/* matmul_plan (gemm.rs:1092-1119): out[m, n] = x[m, k] . W^T with an explicit plan.
+ * x_len / out_len are element counts of the caller's buffers (checked like gemm.rs:1137,1218).
+ * `scratch` may be NULL when plan.splits == 1 and x is bf16 or f16. */
+jk_status jk_matmul_plan(const jk_qmatrix *w, const void *x, int x_dtype, size_t x_len, size_t m,
+                         float *out, size_t out_len, jk_split_scratch *scratch, jk_plan plan,
+                         void *stream);
+
+/* matmul (gemm.rs:1069-1088): matmul_plan with Plan::heuristic(w, m, false, sms). */
+jk_status jk_matmul(const jk_qmatrix *w, const void *x, int x_dtype, size_t x_len, size_t m,
+                    float *out, size_t out_len, jk_split_scratch *scratch, void *stream);
+
+/* matvec (gemm.rs:1135-1168): the small-row kernel, m <= JK_GEMV_ROWS. */
+jk_status jk_matvec(const jk_qmatrix *w, const void *x, int x_dtype, size_t x_len, size_t m,
+                    float *out, size_t out_len, void *stream);
+
+/* matmul_tiled (gemm.rs:1121-1133): matmul_plan with splits = 1. */
+jk_status jk_matmul_tiled(const jk_qmatrix *w, const void *x, int x_dtype, size_t x_len, size_t m,
+                          float *out, size_t out_len, int bm, int bn, void *stream);
+
+/* jevons_burn::kernels::f16_linear / GemmOps::f16_matmul (crates/jevons-burn/src/kernels.rs:
+ * 47-114): out[m, n] f32 = x[m, k] (FP16, dense row-major) . W[n, k]^T (FP16) with the fixed
+ * row-invariant plan of kernels.rs:16-31. */
+jk_status jk_f16_linear(const void *x_f16, size_t m, size_t k, const void *w_f16, size_t n,
+                        float *out, void *stream);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* JK_H */

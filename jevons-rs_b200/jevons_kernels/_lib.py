@@ -1,0 +1,93 @@
+"""ctypes binding of libjk.so (the C ABI declared in include/jk.h).
+
+The library is the product: there is no CPU or PyTorch fallback. If libjk.so is missing or
+fails to load, every entry point raises.
+"""
+from __future__ import annotations
+
+import ctypes
+import os
+
+HERE = os.path.dirname(os.path.abspath(__file__))
+LIB_PATH = os.path.join(HERE, "libjk.so")
+
+# Every symbol include/jk.h declares, with (restype, argtypes).
+P, S, I, U32, U64 = ctypes.c_void_p, ctypes.c_size_t, ctypes.c_int, ctypes.c_uint32, ctypes.c_uint64
+
+
+class Plan(ctypes.Structure):
+    """Plan (crates/jevons-kernels/src/gemm.rs:973-979): bm == 0 selects the small-row kernel."""
+
+    _fields_ = [("bm", ctypes.c_int32), ("bn", ctypes.c_int32), ("splits", ctypes.c_int32)]
+
+    def __repr__(self):
+        return f"Plan(bm={self.bm}, bn={self.bn}, splits={self.splits})"
+
+    def __eq__(self, other):
+        return isinstance(other, Plan) and (self.bm, self.bn, self.splits) == (other.bm, other.bn, other.splits)
+
+    def __hash__(self):
+        return hash((self.bm, self.bn, self.splits))
+
+
+SIGNATURES = {
+    "jk_last_error": (ctypes.c_char_p, []),
+    "jk_abi_version": (I, []),
+    "jk_tensor_type_block": (I, [I, ctypes.POINTER(U64), ctypes.POINTER(U64)]),
+    "jk_q4k_scale_min": (I, [I, P, ctypes.POINTER(ctypes.c_uint8), ctypes.POINTER(ctypes.c_uint8)]),
+    "jk_packed_words": (I, [I, P]),
+    "jk_pack": (I, [I, P, S, P, S, P, S, P, S, P, S]),
+    "jk_gpu_init": (I, [I]),
+    "jk_gpu_sync": (I, [P]),
+    "jk_device_error": (I, [I, ctypes.POINTER(U32)]),
+    "jk_qmatrix_upload": (I, [I, I, S, S, S, P, S, ctypes.POINTER(P)]),
+    "jk_qmatrix_from_packed": (I, [I, I, S, S, S, P, S, P, S, P, S, P, S, ctypes.POINTER(P)]),
+    "jk_qmatrix_f16_view": (I, [I, S, S, P, ctypes.POINTER(P)]),
+    "jk_qmatrix_destroy": (None, [P]),
+    "jk_qmatrix_info": (I, [P, ctypes.POINTER(I), ctypes.POINTER(S), ctypes.POINTER(S), ctypes.POINTER(S),
+                            ctypes.POINTER(S)]),
+    "jk_qmatrix_dequantize": (I, [P, P, S, P]),
+    "jk_plan_heuristic": (I, [P, S, I, I, ctypes.POINTER(Plan)]),
+    "jk_plan_valid_for": (I, [ctypes.POINTER(Plan), P, S]),
+    "jk_split_scratch_create": (I, [I, ctypes.POINTER(P)]),
+    "jk_split_scratch_destroy": (None, [P]),
+    "jk_matmul_plan": (I, [P, P, I, S, S, P, S, P, Plan, P]),
+    "jk_matmul": (I, [P, P, I, S, S, P, S, P, P]),
+    "jk_matvec": (I, [P, P, I, S, S, P, S, P]),
+    "jk_matmul_tiled": (I, [P, P, I, S, S, P, S, I, I, P]),
+    "jk_f16_linear": (I, [P, S, S, P, S, P, P]),
+}
+
+STATUS = {0: "JK_OK", 1: "JK_ERR_INVALID", 2: "JK_ERR_UNSUPPORTED", 3: "JK_ERR_SHAPE", 4: "JK_ERR_CUDA",
+          5: "JK_ERR_NCCL", 6: "JK_ERR_TIMEOUT"}
+
+
+class JkError(RuntimeError):
+    """A failing jk_* call: `status` is the jk_status code, the message is jk_last_error()."""
+
+    def __init__(self, status: int, message: str):
+        super().__init__(f"{STATUS.get(status, status)}: {message}")
+        self.status = status
+        self.message = message
+
+
+_lib = None
+
+
+def load() -> ctypes.CDLL:
+    global _lib
+    if _lib is None:
+        if not os.path.exists(LIB_PATH):
+            raise ImportError(f"libjk.so is not built ({LIB_PATH}); run jevons-rs_b200/build.py")
+        lib = ctypes.CDLL(LIB_PATH)
+        for name, (res, args) in SIGNATURES.items():
+            fn = getattr(lib, name)
+            fn.restype = res
+            fn.argtypes = args
+        _lib = lib
+    return _lib
+
+
+def check(status: int) -> None:
+    if status != 0:
+        raise JkError(status, load().jk_last_error().decode("utf-8", "replace"))

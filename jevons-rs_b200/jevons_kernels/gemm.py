@@ -1,0 +1,290 @@
+"""Quantized-weight matrix products -- the `jevons-kernels` API over libjk.so.
+
+Mirrors crates/jevons-kernels/src/lib.rs:17-303 (`Gpu`, `Buf`) and
+crates/jevons-kernels/src/gemm.rs:817-1321 (`QMatrix`, `Plan`, `SplitScratch`, `matmul`,
+`matmul_plan`, `matvec`, `matmul_tiled`, `GEMV_ROWS`) plus
+crates/jevons-burn/src/kernels.rs:99-129 (`f16_linear`, `f16_linear_scaled`):
+
+    out[r, c] = sum_k x[r, k] * W[c, k]     x: [m, k] (f16 / bf16 / f32), W: [experts * n, k], out f32 [m, n]
+
+Device memory and streams come from PyTorch (plumbing only); every product runs in the CUDA
+kernels of libjk.so, launched asynchronously on the current torch stream. Errors raise JkError
+with the library's message (the reference returns Err(String) or panics).
+"""
+from __future__ import annotations
+
+import ctypes
+
+import numpy as np
+import torch
+
+from ._lib import JkError, Plan, check, load
+from .formats import Packed, TensorType, block, pack
+
+GEMV_ROWS = 16  # gemm.rs:1019
+
+_DTYPE = {torch.float32: 0, torch.float16: 1, torch.bfloat16: 2}
+
+
+def _stream():
+    return ctypes.c_void_p(torch.cuda.current_stream().cuda_stream)
+
+
+class Gpu:
+    """One CUDA device (Gpu::new, lib.rs:181-191): checks it is a B200 (sm_100) and selects it."""
+
+    def __init__(self, device: int = 0):
+        check(load().jk_gpu_init(int(device)))
+        self.device = int(device)
+        torch.cuda.set_device(self.device)
+
+    @staticmethod
+    def new(device: int = 0) -> "Gpu":
+        return Gpu(device)
+
+    def sync(self) -> None:
+        """Blocks until all queued work of the current stream has completed (lib.rs:300-302)."""
+        check(load().jk_gpu_sync(_stream()))
+
+    def torch_device(self) -> torch.device:
+        return torch.device("cuda", self.device)
+
+    def device_error(self) -> int:
+        """Reads and clears the device-side error word (0 = clean)."""
+        code = ctypes.c_uint32()
+        check(load().jk_device_error(self.device, ctypes.byref(code)))
+        return code.value
+
+    # uploads / reads (lib.rs:198-289), in terms of torch tensors
+    def upload_f32(self, data) -> "Buf":
+        return Buf(torch.as_tensor(np.asarray(data, np.float32)).to(self.torch_device()))
+
+    def upload_f16(self, data) -> "Buf":
+        return Buf(torch.as_tensor(np.asarray(data, np.float32)).to(self.torch_device()).half())
+
+    def upload_bf16(self, data) -> "Buf":
+        return Buf(torch.as_tensor(np.asarray(data, np.float32)).to(self.torch_device()).bfloat16())
+
+    def zeros(self, len_: int, dtype=torch.float32) -> "Buf":
+        return Buf(torch.zeros(max(int(len_), 1), dtype=dtype, device=self.torch_device()), int(len_))
+
+    def empty(self, len_: int, dtype=torch.float32) -> "Buf":
+        return Buf(torch.empty(max(int(len_), 1), dtype=dtype, device=self.torch_device()), int(len_))
+
+    def read_f32(self, buf: "Buf") -> np.ndarray:
+        return buf.tensor[: buf.len()].float().cpu().numpy()
+
+
+class Buf:
+    """A device allocation with a logical element count (Buf, lib.rs:75-124): a torch tensor."""
+
+    def __init__(self, tensor: torch.Tensor, len_: int | None = None):
+        if not tensor.is_cuda:
+            raise JkError(1, "Buf must live on a CUDA device")
+        self.tensor = tensor.contiguous().view(-1) if not tensor.is_contiguous() else tensor.view(-1)
+        self._len = self.tensor.numel() if len_ is None else int(len_)
+
+    @staticmethod
+    def from_tensor(t: torch.Tensor) -> "Buf":
+        return Buf(t)
+
+    def len(self) -> int:
+        return self._len
+
+    def is_empty(self) -> bool:
+        return self._len == 0
+
+    def with_len(self, len_: int) -> "Buf":
+        return Buf(self.tensor, len_)
+
+    def ptr(self):
+        return ctypes.c_void_p(self.tensor.data_ptr())
+
+    def dtype_code(self) -> int:
+        try:
+            return _DTYPE[self.tensor.dtype]
+        except KeyError:
+            raise JkError(1, f"unsupported activation dtype {self.tensor.dtype}") from None
+
+
+class QMatrix:
+    """Quantized weights [experts * n, k] resident on the device (gemm.rs:817-953)."""
+
+    def __init__(self, handle, keepalive=None):
+        self._h = ctypes.c_void_p(handle)
+        self._keep = keepalive
+        t, n, k, e, b = ctypes.c_int(), ctypes.c_size_t(), ctypes.c_size_t(), ctypes.c_size_t(), ctypes.c_size_t()
+        check(load().jk_qmatrix_info(self._h, ctypes.byref(t), ctypes.byref(n), ctypes.byref(k), ctypes.byref(e),
+                                     ctypes.byref(b)))
+        self.kind = TensorType(t.value)
+        self.n, self.k, self.experts, self._bytes = n.value, k.value, e.value, b.value
+
+    def __del__(self):
+        h = getattr(self, "_h", None)
+        if h is not None and h.value:
+            try:
+                load().jk_qmatrix_destroy(h)
+            except Exception:
+                pass
+            self._h = ctypes.c_void_p(0)
+
+    @property
+    def handle(self):
+        return self._h
+
+    @staticmethod
+    def upload(gpu: Gpu, kind, n: int, k: int, experts: int, raw) -> "QMatrix":
+        """QMatrix::upload (gemm.rs:832-854): raw GGML bytes -> device, validated and repacked."""
+        arr = np.ascontiguousarray(np.frombuffer(raw, dtype=np.uint8) if isinstance(raw, (bytes, bytearray))
+                                   else np.asarray(raw).view(np.uint8).reshape(-1))
+        out = ctypes.c_void_p()
+        check(load().jk_qmatrix_upload(gpu.device, int(kind), n, k, experts, arr.ctypes.data_as(ctypes.c_void_p),
+                                       arr.size, ctypes.byref(out)))
+        return QMatrix(out.value)
+
+    @staticmethod
+    def from_packed(gpu: Gpu, kind, n: int, k: int, experts: int, p: Packed) -> "QMatrix":
+        """QMatrix::from_packed (gemm.rs:856-899)."""
+        def ptr(a):
+            return a.ctypes.data_as(ctypes.c_void_p) if a.size else None
+        q, h, s = (np.ascontiguousarray(a, np.uint32) for a in (p.q, p.h, p.s))
+        d = np.ascontiguousarray(p.d, np.float32)
+        out = ctypes.c_void_p()
+        check(load().jk_qmatrix_from_packed(gpu.device, int(kind), n, k, experts, ptr(q), q.size, ptr(h), h.size,
+                                            ptr(s), s.size, ptr(d), d.size, ctypes.byref(out)))
+        return QMatrix(out.value)
+
+    @staticmethod
+    def f16_view(gpu: Gpu, n: int, k: int, weights: torch.Tensor) -> "QMatrix":
+        """QMatrix::f16_view (gemm.rs:906-929): row-major FP16 weights [n, k], not copied."""
+        if weights.dtype != torch.float16 or not weights.is_cuda or not weights.is_contiguous():
+            raise JkError(1, "f16_view needs a contiguous FP16 CUDA tensor")
+        if weights.numel() != n * k:
+            raise JkError(3, f"F16 [{n}, {k}] has an unsupported shape")
+        out = ctypes.c_void_p()
+        check(load().jk_qmatrix_f16_view(gpu.device, n, k, ctypes.c_void_p(weights.data_ptr()), ctypes.byref(out)))
+        return QMatrix(out.value, keepalive=weights)
+
+    def bytes(self) -> int:
+        """Device bytes held (QMatrix::bytes, gemm.rs:950-952)."""
+        return self._bytes
+
+    def dequantize(self, out: Buf | None = None) -> torch.Tensor:
+        """Device dequantization to f32 [experts * n, k] (bit-exact with quant::dequantize)."""
+        total = self.experts * self.n * self.k
+        if out is None:
+            dev = torch.device("cuda", torch.cuda.current_device())
+            t = torch.empty(total, dtype=torch.float32, device=dev)
+        else:
+            t = out.tensor
+            if t.dtype != torch.float32:
+                raise JkError(1, "dequantize output must be f32")
+        check(load().jk_qmatrix_dequantize(self._h, ctypes.c_void_p(t.data_ptr()), total if out is None else out.len(),
+                                           _stream()))
+        return t[:total].view(self.experts * self.n, self.k)
+
+
+class SplitScratch:
+    """Device scratch for split-K partial sums, grown on demand (gemm.rs:1040-1065)."""
+
+    def __init__(self, gpu: Gpu | None = None):
+        dev = gpu.device if gpu is not None else torch.cuda.current_device()
+        h = ctypes.c_void_p()
+        check(load().jk_split_scratch_create(dev, ctypes.byref(h)))
+        self._h = h
+
+    def __del__(self):
+        h = getattr(self, "_h", None)
+        if h is not None and h.value:
+            try:
+                load().jk_split_scratch_destroy(h)
+            except Exception:
+                pass
+            self._h = ctypes.c_void_p(0)
+
+    @property
+    def handle(self):
+        return self._h
+
+
+def tile_n(n: int) -> int:
+    """Weight-row tile of the tensor-core kernel (the reference's default column tile, gemm.rs:968-971)."""
+    return 128
+
+
+def _plan_heuristic(w: QMatrix, m: int, row_invariant: bool, groups_target: int = 0) -> Plan:
+    p = Plan()
+    check(load().jk_plan_heuristic(w.handle, m, 1 if row_invariant else 0, int(groups_target), ctypes.byref(p)))
+    return p
+
+
+def _plan_valid_for(self: Plan, w: QMatrix, m: int) -> bool:
+    return bool(load().jk_plan_valid_for(ctypes.byref(self), w.handle, m))
+
+
+Plan.heuristic = staticmethod(_plan_heuristic)
+Plan.valid_for = _plan_valid_for
+Plan.ROW_TILES = (32, 64, 128, 256)
+Plan.COL_TILES = (128,)
+
+
+def _args(x: Buf, out: Buf):
+    return x.ptr(), x.dtype_code(), x.len(), out.ptr(), out.len()
+
+
+def matmul_plan(gpu: Gpu, x: Buf, m: int, w: QMatrix, out: Buf, dummy=None, scratch: SplitScratch | None = None,
+                plan: Plan | None = None) -> None:
+    """matmul_plan (gemm.rs:1092-1119). `dummy` is accepted for signature parity and unused."""
+    xp, xt, xl, op, ol = _args(x, out)
+    check(load().jk_matmul_plan(w.handle, xp, xt, xl, m, op, ol, scratch.handle if scratch else None, plan,
+                                _stream()))
+
+
+def matmul(gpu: Gpu, x: Buf, m: int, w: QMatrix, out: Buf, dummy=None, scratch: SplitScratch | None = None) -> None:
+    """matmul (gemm.rs:1069-1088): the heuristic plan for this device."""
+    xp, xt, xl, op, ol = _args(x, out)
+    check(load().jk_matmul(w.handle, xp, xt, xl, m, op, ol, scratch.handle if scratch else None, _stream()))
+
+
+def matmul_tiled(gpu: Gpu, x: Buf, m: int, w: QMatrix, out: Buf, dummy=None, bm: int = 128, bn: int = 128) -> None:
+    """matmul_tiled (gemm.rs:1121-1133)."""
+    xp, xt, xl, op, ol = _args(x, out)
+    check(load().jk_matmul_tiled(w.handle, xp, xt, xl, m, op, ol, bm, bn, _stream()))
+
+
+def matvec(gpu: Gpu, x: Buf, m: int, w: QMatrix, out: Buf, dummy=None) -> None:
+    """matvec (gemm.rs:1135-1168): m <= GEMV_ROWS."""
+    xp, xt, xl, op, ol = _args(x, out)
+    check(load().jk_matvec(w.handle, xp, xt, xl, m, op, ol, _stream()))
+
+
+def f16_linear(x: torch.Tensor, weight: torch.Tensor) -> torch.Tensor:
+    """jevons_burn::kernels::f16_linear (kernels.rs:107-114): f32 x @ weight^T with FP16 weight [N, K].
+
+    x is cast to FP16 first, so its magnitudes must stay within the FP16 range."""
+    if weight.dtype != torch.float16:
+        raise JkError(1, "f16 matmul needs FP16 operands")
+    x16 = x.to(torch.float16).contiguous()
+    w = weight.contiguous()
+    m, k = x16.shape
+    n = w.shape[0]
+    if w.shape[1] != k:
+        raise JkError(1, "f16 matmul needs dense row-major [M, K] x [N, K]")
+    out = torch.empty(m, n, dtype=torch.float32, device=x16.device)
+    check(load().jk_f16_linear(ctypes.c_void_p(x16.data_ptr()), m, k, ctypes.c_void_p(w.data_ptr()), n,
+                               ctypes.c_void_p(out.data_ptr()), _stream()))
+    return out
+
+
+F16_ROW_LIMIT = 16384.0  # kernels.rs:105
+
+
+def f16_linear_scaled(x: torch.Tensor, weight: torch.Tensor) -> torch.Tensor:
+    """kernels.rs:116-129: rows with max |x| > 16384 are divided down first and scaled back."""
+    x = x.float()
+    scale = (x.abs().amax(dim=1, keepdim=True) / F16_ROW_LIMIT).clamp_min(1.0)
+    return f16_linear(x / scale, weight) * scale
+
+
+__all__ = ["GEMV_ROWS", "Gpu", "Buf", "QMatrix", "Plan", "SplitScratch", "matmul", "matmul_plan", "matmul_tiled",
+           "matvec", "f16_linear", "f16_linear_scaled", "tile_n", "TensorType", "block", "pack", "JkError"]

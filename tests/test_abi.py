@@ -1,0 +1,106 @@
+"""CPU tests of the C ABI boundary: libjk.so loads, exports every symbol include/jk.h declares,
+and its host-side validation answers like the reference (no GPU calls)."""
+import ctypes
+import os
+import re
+
+import numpy as np
+import pytest
+
+from jevons_kernels import _lib
+from jevons_kernels._lib import JkError, check, load
+
+REPO = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
+HEADER = os.path.join(REPO, "include", "jk.h")
+
+
+def declared_symbols():
+    src = open(HEADER).read()
+    src = re.sub(r"/\*.*?\*/", "", src, flags=re.S)
+    return sorted(set(re.findall(r"\b(jk_[a-z0-9_]+)\s*\(", src)))
+
+
+def test_header_declares_the_expected_entry_points():
+    syms = declared_symbols()
+    for name in ("jk_qmatrix_upload", "jk_matmul_plan", "jk_matvec", "jk_f16_linear", "jk_pack",
+                 "jk_plan_heuristic", "jk_qmatrix_dequantize", "jk_last_error"):
+        assert name in syms
+
+
+def test_library_exports_every_declared_symbol():
+    lib = ctypes.CDLL(_lib.LIB_PATH)
+    missing = [s for s in declared_symbols() if not hasattr(lib, s)]
+    assert not missing, f"libjk.so lacks {missing}"
+
+
+def test_python_binding_covers_every_declared_symbol():
+    assert set(declared_symbols()) <= set(_lib.SIGNATURES), set(declared_symbols()) - set(_lib.SIGNATURES)
+
+
+def test_abi_version():
+    assert load().jk_abi_version() == 1
+
+
+def upload(kind, n, k, experts, raw):
+    out = ctypes.c_void_p()
+    arr = np.frombuffer(bytes(raw), np.uint8) if len(raw) else np.zeros(1, np.uint8)
+    st = load().jk_qmatrix_upload(0, kind, n, k, experts, arr.ctypes.data_as(ctypes.c_void_p), len(raw),
+                                  ctypes.byref(out))
+    return st, load().jk_last_error().decode()
+
+
+def test_upload_rejects_wrong_byte_count_with_reference_message():
+    # gemm.rs:841-845: "{kind:?} [{experts}x{n}, {k}] has the wrong byte count"
+    st, msg = upload(12, 64, 256, 1, bytes(144 * 64 - 1))
+    assert st == 3 and msg == "Q4K [1x64, 256] has the wrong byte count"
+
+
+def test_upload_rejects_unsupported_shape_with_reference_message():
+    # gemm.rs:875-885: n % 64 and k % 64 -> "... has an unsupported shape"
+    st, msg = upload(8, 32, 64, 1, bytes(34 * 2 * 32))
+    assert st == 3 and msg == "Q8_0 [1x32, 64] has an unsupported shape"
+    st, msg = upload(8, 64, 96, 1, bytes(34 * 3 * 64))
+    assert st == 3 and msg == "Q8_0 [1x64, 96] has an unsupported shape"
+
+
+def test_upload_rejects_types_without_gpu_layout():
+    st, msg = upload(0, 64, 64, 1, bytes(4 * 64 * 64))
+    assert st == 2 and "not supported" in msg
+    st, msg = upload(2, 64, 64, 1, bytes(16))
+    assert st == 2
+
+
+def test_errors_are_thread_local_messages():
+    import threading
+    seen = {}
+
+    def worker():
+        seen["msg"] = upload(12, 64, 256, 1, bytes(10))[1]
+    upload(8, 32, 64, 1, bytes(34 * 2 * 32))
+    t = threading.Thread(target=worker)
+    t.start()
+    t.join()
+    assert "Q4K" in seen["msg"]
+    assert load().jk_last_error().decode().startswith("Q8_0")
+
+
+def test_check_raises_jkerror():
+    st, _ = upload(12, 64, 256, 1, bytes(1))
+    with pytest.raises(JkError) as e:
+        check(st)
+    assert e.value.status == 3 and "wrong byte count" in str(e.value)
+
+
+def test_q4k_scale_min_rejects_out_of_range_j():
+    sc, mn = ctypes.c_uint8(), ctypes.c_uint8()
+    buf = (ctypes.c_uint8 * 12)()
+    assert load().jk_q4k_scale_min(8, buf, ctypes.byref(sc), ctypes.byref(mn)) == 1
+
+
+def test_pack_rejects_small_regions():
+    raw = np.zeros(34, np.uint8)
+    q = np.zeros(7, np.uint32)
+    d = np.zeros(1, np.float32)
+    st = load().jk_pack(8, raw.ctypes.data_as(ctypes.c_void_p), 34, q.ctypes.data_as(ctypes.c_void_p), 7, None, 0,
+                        None, 0, d.ctypes.data_as(ctypes.c_void_p), 1)
+    assert st == 1

@@ -1,0 +1,216 @@
+"""GPU: the tcgen05 tensor-core product (matmul_plan / matmul / matmul_tiled, gemm.rs:1067-1257)
+against the f64 oracle, every valid plan, bitwise row invariance, edge shapes and the BASELINE
+configurations. Mirrors crates/jevons-gemma4-diffusion/src/gpu/tests.rs:427-480."""
+import numpy as np
+import pytest
+import torch
+
+from helpers import KINDS, activations, assert_close, make_weights
+from oracle import oracle
+from jevons_kernels import synth
+
+pytestmark = pytest.mark.gpu
+
+M_CASES = [3, 16, 70, 150, 300]
+
+
+def all_plans(w, m):
+    from jevons_kernels.gemm import Plan
+    plans = [Plan(0, 128, 1)]
+    for bm in Plan.ROW_TILES:
+        for splits in (1, 2, 8):
+            plans.append(Plan(bm, 128, splits))
+    return [p for p in plans if p.valid_for(w, m)]
+
+
+@pytest.mark.parametrize("dtype", [torch.float16, torch.bfloat16])
+@pytest.mark.parametrize("name,k", [("Q8_0", 512), ("Q4_K", 512), ("Q6_K", 512), ("Q5_0", 512)])
+def test_every_plan_matches_oracle_and_tiles_are_row_invariant(gpu, name, k, dtype):
+    from jevons_kernels.gemm import Buf, SplitScratch, matmul_plan
+    n = 256
+    w, raw, dense = make_weights(gpu, KINDS[name], n, k, seed=11)
+    scratch = SplitScratch(gpu)
+    for m in M_CASES:
+        x, x_exact = activations(m, k, dtype, seed=m)
+        want = oracle.matmul_f64(x_exact, dense)
+        reference = None
+        for plan in all_plans(w, m):
+            out = torch.full((m, n), float("nan"), device="cuda")
+            matmul_plan(gpu, Buf(x), m, w, Buf(out), None, scratch, plan)
+            got = out.cpu().numpy()
+            assert_close(f"{name} m={m} {plan} {dtype}", got, x_exact, dense, want, ref_rule=dtype == torch.float16)
+            if plan.bm > 0 and plan.splits == 1:
+                # Tile shape must not change any row's accumulation order (tests.rs:470-477).
+                if reference is None:
+                    reference = got
+                else:
+                    assert np.array_equal(reference.view(np.uint32), got.view(np.uint32)), f"{name} m={m} {plan}"
+    assert gpu.device_error() == 0
+
+
+@pytest.mark.parametrize("name", ["Q4_K", "Q8_0"])
+def test_rows_are_invariant_across_m(gpu, name):
+    """Row-invariant plans give every row the same bits whatever m is (prefix reuse, gemm.rs:1090)."""
+    from jevons_kernels.gemm import Buf, Plan, matmul_plan
+    n, k = 384, 1024
+    w, _, _ = make_weights(gpu, KINDS[name], n, k, seed=2)
+    x, _ = activations(300, k, torch.bfloat16, seed=4)
+    full = torch.empty(300, n, device="cuda")
+    matmul_plan(gpu, Buf(x), 300, w, Buf(full), None, None, Plan(256, 128, 1))
+    for m in (1, 5, 33, 129):
+        part = torch.empty(m, n, device="cuda")
+        matmul_plan(gpu, Buf(x[:m].contiguous()), m, w, Buf(part), None, None, Plan(64, 128, 1))
+        assert torch.equal(part, full[:m]), m
+
+
+@pytest.mark.parametrize("dtype", [torch.float16, torch.float32])
+@pytest.mark.parametrize("name", ["Q4_K", "Q6_K", "Q8_0"])
+def test_activation_dtypes(gpu, name, dtype):
+    from jevons_kernels.gemm import Buf, Plan, SplitScratch, matmul_plan
+    n, k, m = 256, 512, 96
+    w, _, dense = make_weights(gpu, KINDS[name], n, k, seed=5)
+    x, x_exact = activations(m, k, dtype, seed=6)
+    if dtype == torch.float32:
+        x_exact = synth.bf16_round(x_exact)  # f32 activations are rounded to bf16 for the MMA
+    out = torch.empty(m, n, device="cuda")
+    matmul_plan(gpu, Buf(x), m, w, Buf(out), None, SplitScratch(gpu), Plan(128, 128, 2))
+    assert_close(f"{name} {dtype}", out.cpu().numpy(), x_exact, dense)
+
+
+@pytest.mark.parametrize("name,n,k", [("Q8_0", 64, 64), ("Q8_0", 192, 320), ("Q4_K", 64, 256), ("Q6_K", 320, 768),
+                                      ("Q5_0", 64, 128), ("Q4_K", 192, 2560)])
+@pytest.mark.parametrize("m", [1, 31, 33, 257])
+def test_ragged_shapes(gpu, name, n, k, m):
+    """Partial weight tiles (n % 128 != 0), partial row tiles, partial super-block stages."""
+    from jevons_kernels.gemm import Buf, Plan, matmul_plan
+    w, _, dense = make_weights(gpu, KINDS[name], n, k, seed=n + k)
+    x, x_exact = activations(m, k, torch.bfloat16, seed=m)
+    for bm in (32, 256):
+        # one spare row after the output must stay untouched
+        out = torch.full((m + 1, n), float("nan"), device="cuda")
+        matmul_plan(gpu, Buf(x), m, w, Buf(out), None, None, Plan(bm, 128, 1))
+        assert_close(f"{name} {n}x{k} m={m} bm={bm}", out[:m].cpu().numpy(), x_exact, dense)
+        assert torch.isnan(out[m]).all()
+
+
+def test_multi_expert_matrix_dense_product_uses_expert_zero(gpu):
+    from jevons_kernels.gemm import Buf, Plan, matmul_plan
+    n, k, e, m = 128, 512, 3, 40
+    w, _, dense = make_weights(gpu, KINDS["Q4_K"], n, k, experts=e, seed=8)
+    x, x_exact = activations(m, k, torch.bfloat16, seed=9)
+    out = torch.empty(m, n, device="cuda")
+    matmul_plan(gpu, Buf(x), m, w, Buf(out), None, None, Plan(64, 128, 1))
+    assert_close("expert 0", out.cpu().numpy(), x_exact, dense[:n])
+
+
+def test_heuristic_plans_and_matmul(gpu):
+    from jevons_kernels.gemm import Buf, Plan, SplitScratch, matmul
+    w, _, dense = make_weights(gpu, KINDS["Q4_K"], 10240, 2560, seed=1)
+    for m, want in ((1, 0), (2, 0), (32, 32), (256, 256)):
+        p = Plan.heuristic(w, m, False)
+        assert p.bm == want and p.valid_for(w, m)
+        assert Plan.heuristic(w, m, True).splits == 1 and Plan.heuristic(w, m, True).bm > 0
+    x, x_exact = activations(32, 2560, torch.bfloat16, seed=1)
+    out = torch.empty(32, 10240, device="cuda")
+    matmul(gpu, Buf(x), 32, w, Buf(out), None, SplitScratch(gpu))
+    assert_close("cfg1 heuristic", out.cpu().numpy(), x_exact, dense)
+
+
+def test_plan_validation(gpu):
+    from jevons_kernels.gemm import Buf, JkError, Plan, matmul_plan
+    w, _, _ = make_weights(gpu, KINDS["Q8_0"], 128, 256)
+    assert not Plan(48, 128, 1).valid_for(w, 4)
+    assert not Plan(64, 64, 1).valid_for(w, 4)
+    assert not Plan(64, 128, 8).valid_for(w, 4)  # k/64 = 4 < 8 splits
+    assert not Plan(0, 128, 1).valid_for(w, 17)
+    x = torch.zeros(4, 256, device="cuda", dtype=torch.bfloat16)
+    with pytest.raises(JkError, match="not valid"):
+        matmul_plan(gpu, Buf(x), 4, w, Buf(torch.zeros(4, 128, device="cuda")), None, None, Plan(48, 128, 1))
+    with pytest.raises(JkError, match="scratch"):
+        matmul_plan(gpu, Buf(x), 4, w, Buf(torch.zeros(4, 128, device="cuda")), None, None, Plan(64, 128, 2))
+
+
+# --- FP16 weights: the Burn-facing f16_linear (crates/jevons-burn/src/kernels.rs:131-309) ---------
+
+@pytest.mark.parametrize("m,n,k", [(32, 64, 256), (32, 4160, 512), (64, 256, 1024), (512, 384, 512),
+                                   (32, 6144, 4096), (128, 4096, 4096), (32, 131136, 4096)])
+def test_f16_linear_matches_f32_matmul(gpu, m, n, k):
+    from jevons_kernels.gemm import f16_linear
+    g = torch.Generator(device="cuda").manual_seed(m * 7 + n)
+    x = (torch.rand(m, k, device="cuda", generator=g) * 2 - 1).half()
+    w = ((torch.rand(n, k, device="cuda", generator=g) * 2 - 1) * 0.1).half()
+    want = x.float() @ w.float().t()
+    got = f16_linear(x, w)
+    worst = (want - got).abs().max().item()
+    scale = want.abs().max().item()
+    assert worst <= 2e-3 * max(scale, 1.0), (m, n, k, worst)
+
+
+def test_f16_outputs_beyond_the_fp16_range_stay_exact(gpu):
+    from jevons_kernels.gemm import f16_linear
+    m, n, k = 128, 256, 4096
+    g = torch.Generator(device="cuda").manual_seed(3)
+    x = torch.rand(m, k, device="cuda", generator=g) * 2 + 29
+    w = (torch.rand(n, k, device="cuda", generator=g) * 0.2 + 0.9).half()
+    want = x.half().float() @ w.float().t()
+    got = f16_linear(x, w)
+    worst = (want - got).abs().max().item()
+    assert worst <= want[0, 0].abs().item() * 1e-3
+
+
+def test_f16_linear_scaled_handles_huge_rows(gpu):
+    from jevons_kernels.gemm import f16_linear_scaled
+    m, n, k = 32, 128, 256
+    x = torch.randn(m, k, device="cuda")
+    x[3] *= 1e6
+    w = (torch.randn(n, k, device="cuda") * 0.05).half()
+    want = x @ w.float().t()
+    got = f16_linear_scaled(x, w)
+    rel = ((want - got).abs().max(dim=1).values / want.abs().max(dim=1).values).max().item()
+    assert rel < 2e-3
+
+
+# --- BASELINE configurations -------------------------------------------------------------------
+
+def test_config1_q4k_m32(gpu):
+    """Q4_K M=32, K=2560 -> N=10240, bf16 activations, full size vs oracle."""
+    from jevons_kernels.gemm import Buf, Plan, matmul_plan
+    w, _, dense = make_weights(gpu, KINDS["Q4_K"], 10240, 2560, seed=1)
+    x, x_exact = activations(32, 2560, torch.bfloat16, seed=1)
+    out = torch.empty(32, 10240, device="cuda")
+    matmul_plan(gpu, Buf(x), 32, w, Buf(out), None, None, Plan(32, 128, 1))
+    assert_close("cfg1", out.cpu().numpy(), x_exact, dense)
+
+
+def test_config2_q6k_m256(gpu):
+    """Q6_K M=256, K=10240 -> N=2560, bf16 activations ~N(0, 0.5)."""
+    from jevons_kernels.gemm import Buf, Plan, SplitScratch, matmul_plan
+    w, _, dense = make_weights(gpu, KINDS["Q6_K"], 2560, 10240, seed=2)
+    x, x_exact = activations(256, 10240, torch.bfloat16, seed=2, sigma=0.5)
+    out = torch.empty(256, 2560, device="cuda")
+    for plan in (Plan(256, 128, 1), Plan.heuristic(w, 256, False)):
+        matmul_plan(gpu, Buf(x), 256, w, Buf(out), None, SplitScratch(gpu), plan)
+        assert_close(f"cfg2 {plan}", out.cpu().numpy(), x_exact, dense)
+
+
+def test_config4_vocab_head_sampled_and_linear(gpu):
+    """Q4_K vocab head M=2048, K=2560 -> N=262144: a sampled block of outputs
+    against the oracle, and linearity out(a + b) == out(a) + out(b) within tolerance."""
+    from jevons_kernels.gemm import Buf, Plan, matmul_plan
+    n, k, m = 262144, 2560, 2048
+    rng = np.random.default_rng(4)
+    raw = synth.q4k_blocks(rng, n, k)
+    from jevons_kernels.gemm import QMatrix
+    w = QMatrix.upload(gpu, oracle.Q4_K, n, k, 1, raw)
+    x, x_exact = activations(m, k, torch.bfloat16, seed=4)
+    out = torch.empty(m, n, device="cuda")
+    matmul_plan(gpu, Buf(x), m, w, Buf(out), None, None, Plan(256, 128, 1))
+    cols = np.sort(rng.choice(n, 300, replace=False))
+    rows = np.sort(rng.choice(m, 40, replace=False))
+    dense_cols = oracle.dequantize(oracle.Q4_K, raw.reshape(n, -1)[cols]).reshape(len(cols), k)
+    got = out[torch.from_numpy(rows).cuda()][:, torch.from_numpy(cols).cuda()].cpu().numpy()
+    assert_close("cfg4 sample", got, x_exact[rows], dense_cols)
+    # linearity on exact-in-bf16 halves: a = x, b = x (so a + b = 2x exactly) -> out(2x) == 2 out(x)
+    out2 = torch.empty_like(out)
+    matmul_plan(gpu, Buf((x * 2).contiguous()), m, w, Buf(out2), None, None, Plan(256, 128, 1))
+    assert torch.equal(out2, out * 2)

@@ -1,0 +1,147 @@
+"""CPU tests: the oracle is pinned to the reference's known answers and to a second restatement,
+and the product's host-side format functions agree with it. No GPU needed."""
+import json
+import os
+
+import numpy as np
+import pytest
+
+from oracle import oracle
+from jevons_kernels import formats, synth
+
+HERE = os.path.dirname(os.path.abspath(__file__))
+KAT = json.load(open(os.path.join(HERE, "golden", "quant_kat.json")))
+TYPES = [("q4k", oracle.Q4_K, 512), ("q6k", oracle.Q6_K, 512), ("q8_0", oracle.Q8_0, 128), ("q5_0", oracle.Q5_0, 128)]
+
+
+# --- known answers from crates/jevons-formats/src/quant.rs:199-237 --------------------------------
+
+@pytest.mark.parametrize("impl", ["oracle", "product"])
+def test_q4k_decodes_scale_high_bits_for_upper_groups(impl):
+    case = KAT["q4k_scale_min"]
+    fn = oracle.q4k_scale_min if impl == "oracle" else formats.q4k_scale_min
+    for j, want in case["expect"].items():
+        assert fn(int(j), bytes(case["scales"])) == tuple(want)
+
+
+def test_q8_0_and_q5_0_dequantize_signed_values():
+    for name in ("q8_0", "q5_0"):
+        case = KAT[name]
+        out = oracle.dequantize(case["type"], bytes(case["bytes"]))
+        for i, want in case["expect"].items():
+            assert out[int(i)] == want, (name, i, out[int(i)], want)
+
+
+@pytest.mark.parametrize("impl", ["oracle", "product"])
+def test_packing_splits_quants_and_scales_without_changing_values(impl):
+    case = KAT["pack_q8_0"]
+    raw = bytes(case["bytes"])
+    if impl == "oracle":
+        q, h, s, d = oracle.pack(case["type"], raw)
+        with pytest.raises(oracle.OracleError):
+            oracle.pack(case["type"], raw[: case["bad_len"]])
+    else:
+        p = formats.pack(case["type"], raw)
+        q, d = p.q, p.d
+        from jevons_kernels._lib import JkError
+        with pytest.raises(JkError):
+            formats.pack(case["type"], raw[: case["bad_len"]])
+    assert len(q) == case["q_len"] and list(d) == case["d"]
+    assert int(q[0]) == case["q0"]
+
+
+def test_dequantize_rejects_bad_sizes_and_types():
+    with pytest.raises(oracle.OracleError):
+        oracle.dequantize(oracle.Q8_0, bytes(33))
+    with pytest.raises(oracle.OracleError):
+        oracle.dequantize(oracle.Q8_0, bytes(34), out_len=31)
+    with pytest.raises(oracle.OracleError):
+        oracle.dequantize(99, bytes(34))
+
+
+def test_block_sizes_match_gguf():
+    # TensorType::block (gguf.rs:134-145)
+    want = {0: (1, 4), 1: (1, 2), 12: (256, 144), 6: (32, 22), 14: (256, 210), 8: (32, 34)}
+    for t, wb in want.items():
+        assert oracle.block(t) == wb
+        assert formats.block(t) == wb
+    assert oracle.block(2) is None and formats.block(2) is None
+
+
+# --- the oracle against a second restatement (the reference's GPU word decode) --------------------
+
+@pytest.mark.parametrize("name,kind,k", TYPES)
+def test_oracle_matches_word_level_decode_bit_exact(name, kind, k):
+    rng = np.random.default_rng(7)
+    raw = synth.weights(kind, rng, 64, k)
+    a = oracle.dequantize(kind, raw)
+    b = oracle.dequantize_words(kind, raw)
+    assert a.view(np.uint32).tolist() == b.view(np.uint32).tolist()
+
+
+@pytest.mark.parametrize("name,kind,k", TYPES)
+def test_oracle_matches_word_level_decode_on_random_bytes(name, kind, k):
+    # Arbitrary bytes (any scale, NaN/inf halves included) must decode identically too.
+    rng = np.random.default_rng(11)
+    size = oracle.block(kind)[1]
+    raw = rng.integers(0, 256, size=size * 97, dtype=np.uint8)
+    a = oracle.dequantize(kind, raw)
+    b = oracle.dequantize_words(kind, raw)
+    assert np.array_equal(a.view(np.uint32), b.view(np.uint32))
+
+
+def test_oracle_regression_vectors():
+    v = np.load(os.path.join(HERE, "golden", "oracle_vectors.npz"))
+    for name, kind, _ in TYPES:
+        got = oracle.dequantize(kind, v[f"{name}_raw"])
+        assert np.array_equal(got.view(np.uint32), v[f"{name}_f32"].view(np.uint32)), name
+
+
+def test_half_conversion_is_exact():
+    bits = np.arange(0, 1 << 16, 97, dtype=np.uint16)
+    want = bits.view(np.float16).astype(np.float32)
+    got = np.array([oracle.half_to_float(int(b)) for b in bits], np.float32)
+    finite = np.isfinite(want)
+    assert np.array_equal(got[finite].view(np.uint32), want[finite].view(np.uint32))
+    assert np.all(np.isnan(got[~finite]) == np.isnan(want[~finite]))
+
+
+# --- product host repacking == oracle pack ---------------------------------------------------------
+
+@pytest.mark.parametrize("name,kind,k", TYPES)
+def test_product_pack_equals_oracle_pack(name, kind, k):
+    rng = np.random.default_rng(3)
+    raw = synth.weights(kind, rng, 8, k)
+    q, h, s, d = oracle.pack(kind, raw)
+    p = formats.pack(kind, raw)
+    assert np.array_equal(q, p.q) and np.array_equal(h, p.h) and np.array_equal(s, p.s)
+    assert np.array_equal(d.view(np.uint32), p.d.view(np.uint32))
+    assert formats.packed_words(kind) == oracle.packed_words(kind)
+
+
+# --- synthetic generators --------------------------------------------------------------------------
+
+def test_q4k_generator_ranges():
+    rng = np.random.default_rng(0)
+    raw = synth.q4k_blocks(rng, 4, 1024).reshape(-1, 144)
+    for blk in raw[:8]:
+        for j in range(8):
+            sc, mn = oracle.q4k_scale_min(j, bytes(blk[4:16]))
+            assert 0 <= sc < 64 and 0 <= mn < 64
+
+
+def test_q4k_scale_packing_roundtrip():
+    rng = np.random.default_rng(1)
+    sc = rng.integers(0, 64, (50, 8))
+    mn = rng.integers(0, 64, (50, 8))
+    packed = synth.q4k_scales(sc, mn)
+    for b in range(50):
+        for j in range(8):
+            assert oracle.q4k_scale_min(j, bytes(packed[b])) == (sc[b, j], mn[b, j])
+
+
+def test_bf16_round_matches_torch():
+    torch = pytest.importorskip("torch")
+    x = np.random.default_rng(2).normal(0, 3, 4096).astype(np.float32)
+    want = torch.from_numpy(x).bfloat16().float().numpy()
+    assert np.array_equal(synth.bf16_round(x), want)

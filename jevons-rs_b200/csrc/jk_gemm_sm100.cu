@@ -1,33 +1,37 @@
 // jk_gemm_sm100.cu -- tensor-core product out[r, c] = sum_j x[r, j] W[c, j] on sm_100a
-// (the reference's `gemm` kernel + `matmul_split`/`reduce_splits`,
-// crates/jevons-kernels/src/gemm.rs:532-815 and :1205-1269), designed for Blackwell:
+// (the reference's `gemm` kernel with `matmul_split` / `reduce_splits`,
+// crates/jevons-kernels/src/gemm.rs:532-815 and :1205-1269), designed for Blackwell.
 //
-//   * Roles are swapped relative to the usual activation-major GEMM: the 5th-generation MMA's
-//     M side (128 TMEM lanes) carries 128 WEIGHT rows and its N side carries BT activation rows
-//     (BT = 32..256), so a 32-row canvas product still fills whole MMAs and the f32 accumulator
-//     tile sits in tensor memory as [weight row][activation row].
-//   * Warp roles (192 threads, one output tile per CTA):
-//       warp 0      TMA producer: activation tiles (bf16/f16, 128-byte swizzled) and raw
-//                   quantized weight tiles (one 256-wide super-block of 128 rows per stage);
-//       warp 1      allocates tensor memory; lane 0 issues tcgen05.mma (4 x K=16 per 64-wide
-//                   k-block) and commits each stage back to the producers;
-//       warps 2..5  dequantize: thread t decodes row t's k-block from the raw stage with the
-//                   exact f32 arithmetic of the reference (jk_decode.cuh), rounds to bf16/f16
-//                   and stores it into the 128-byte-swizzled K-major operand tile; after the
-//                   last k-block the same warps drain the accumulators (tcgen05.ld) and store
-//                   f32 outputs, 128 contiguous bytes per warp store.
-//   * Pipelines: S operand stages guarded by mbarriers (full_b: TMA bytes landed; full_a:
-//     4 dequant warps done; empty: the MMAs reading the stage completed), 2 raw weight stages
-//     (raw_full / raw_empty). Every wait is bounded (4 s); a wait that runs out records an error
-//     code in the per-device error word and the CTA skips its remaining work, drains its
-//     in-flight copies and MMAs, and frees its tensor memory.
-//   * FP16 weights (the Burn-facing f16_linear path) skip dequantization: the producer loads the
-//     weight tile straight into the swizzled operand stage.
-//   * Split-K (grid.z = splits) partitions the 64-wide k-blocks like gemm.rs:573-576 and writes
-//     partial tiles to a scratch buffer, reduced in fixed split order by reduce_splits_kernel.
-//     With splits == 1 each output element's accumulation order is the same for every BT and m
-//     (row invariance, gemm.rs:1090-1091).
-//   * No TMA multicast anywhere.
+// * Roles swapped: the MMA's M side (128 TMEM lanes) carries 128 WEIGHT rows and its N side
+//   carries BT activation rows (BT = 32..256), so a 32-row canvas product still issues full
+//   MMAs; the f32 accumulator tile sits in tensor memory as [weight row][activation row].
+// * Persistent CTAs, one per SM. The work is (tile, 64-wide k-block) iterations. Two schedules:
+//     DP  (row-invariant plans, splits == 1): CTA c takes whole tiles c, c+G, ... -- every
+//         output's accumulation order is the same for any m and any BT;
+//     SK  (splits > 1): CTA c takes the contiguous iteration range [c*T/G, (c+1)*T/G) of all
+//         T = tiles * k-blocks iterations ("stream-K"), so all SMs get equal work whatever the
+//         tile count. A tile split between CTAs is finished by the CTA holding its first
+//         k-block (the owner); the others (contributors) store f32 partial tiles to the split
+//         scratch and raise a flag; the owner adds them in increasing k order (deterministic for
+//         a given shape) and clears the flags for the next launch.
+// * Warp roles (480 threads):
+//     warp 0       TMA producer of the activation tiles (box 64 x BT, 128-byte swizzle);
+//     warp 1       allocates 2 x BT TMEM columns (two accumulator buffers); lane 0 issues
+//                  tcgen05.mma (kind::f16, 4 x K=16 per k-block) and commits stages / tiles;
+//     warp 2       TMA producer of the raw quantized weight stages (one 256-wide super-block of
+//                  128 rows each, 2-4 stages), running ahead of the operand pipeline;
+//     warps 3..6   epilogue: tcgen05.ld of a finished accumulator buffer, f32 stores
+//                  (128 contiguous bytes per warp store), partial-tile handshakes;
+//     warps 7..14  dequantize: 2 threads per weight row decode half a k-block each from the raw
+//                  stage with the exact f32 arithmetic of the reference (jk_decode.cuh), round to
+//                  bf16 (f16 with f16 activations) and store into the 128-byte-swizzled K-major
+//                  operand tile, then fence.proxy.async to hand it to the tensor core.
+//   The epilogue of tile i overlaps the MMAs of tile i+1 (double-buffered accumulators).
+// * Every mbarrier / flag wait is bounded (4 s): on expiry the error word records
+//   ERR_WAIT_TIMEOUT, the CTA stops issuing work, drains what it issued and frees TMEM.
+// * FP16 weights (the Burn-facing f16_linear path) skip dequantization: the producer TMA-loads the
+//   weight tile straight into the swizzled operand stage.
+// * No TMA multicast anywhere.
 #include "jk_decode.cuh"
 #include "jk_internal.h"
 
@@ -37,14 +41,15 @@ namespace jk {
 
 namespace {
 
-constexpr int BW = 128;           // weight rows per tile (MMA M)
-constexpr int KB = 64;            // k-block (one 128-byte swizzle atom of 16-bit values)
-constexpr int THREADS = 192;
-constexpr int A_STAGE_BYTES = BW * KB * 2;  // 16 KB
+constexpr int BW = 128;                  // weight rows per tile (MMA M)
+constexpr int KB = 64;                   // k-block: one 128-byte swizzle atom of 16-bit values
+constexpr int A_STAGE_BYTES = BW * KB * 2;
+constexpr int PRODUCER_WARP = 0, MMA_WARP = 1, RAW_WARP = 2, EPI_WARP0 = 3, EPI_WARPS = 4, DQ_WARP0 = 7, DQ_WARPS = 8;
+constexpr int THREADS = 32 * (DQ_WARP0 + DQ_WARPS);  // 480
+constexpr int EPI_THREADS = 32 * EPI_WARPS;          // 128: 1 per weight row
 
 template <int FMT>
 struct RawTile {
-    // bytes of one raw weight stage (one 256-wide super-block of 128 rows)
     static constexpr int bytes = FMT == FMT_Q4K ? BW * 144
                                : FMT == FMT_Q6K ? BW * 208
                                : FMT == FMT_Q8_0 ? BW * 256
@@ -52,43 +57,332 @@ struct RawTile {
                                : 0;
 };
 
-template <int BT>
-struct Stages {
-    static constexpr int S = BT >= 256 ? 3 : 4;
-};
+constexpr int SMEM_LIMIT = 227 * 1024;
 
 template <int FMT, int BT>
 struct Smem {
-    static constexpr int S = Stages<BT>::S;
+    static constexpr int S = BT >= 256 ? 3 : 4;  // operand stages (activation tile + weight tile)
     static constexpr int B_STAGE = BT * 128;
+    static constexpr int raw_bytes = RawTile<FMT>::bytes;
+    static constexpr int fixed = S * (B_STAGE + A_STAGE_BYTES) + 2048;
+    // raw weight stages: as many as fit (2..4), each one 256-wide super-block of 128 rows
+    static constexpr int R = raw_bytes == 0 ? 1
+                           : (fixed + 4 * raw_bytes <= SMEM_LIMIT ? 4 : fixed + 3 * raw_bytes <= SMEM_LIMIT ? 3 : 2);
     static constexpr int off_b = 0;
     static constexpr int off_a = off_b + S * B_STAGE;
     static constexpr int off_raw = off_a + S * A_STAGE_BYTES;
-    static constexpr int raw_bytes = RawTile<FMT>::bytes;
-    static constexpr int off_bar = off_raw + 2 * raw_bytes;
-    static constexpr int n_bar = 3 * S + 5;
+    static constexpr int off_bar = off_raw + R * raw_bytes;
+    static constexpr int n_bar = 3 * S + 2 * R + 4;  // full_b, full_a, empty | raw_full/empty | acc_full/empty x2
     static constexpr int off_tmem = off_bar + 8 * n_bar;
-    static constexpr int total = off_tmem + 16 + 1024;  // + alignment slack
+    static constexpr int total = off_tmem + 16 + 1024;  // + base alignment slack
+    static_assert(total <= SMEM_LIMIT, "shared memory budget");
 };
 
-__global__ void __launch_bounds__(256) reduce_splits_kernel(const float* __restrict__ part, float* __restrict__ out,
-                                                            int64_t len, int splits) {
-    const int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
-    if (i >= len) return;
-    float s = 0.f;
-    for (int z = 0; z < splits; ++z) s += part[(int64_t)z * len + i];
-    out[i] = s;
+// ------------------------------------------------------------------------------------------------
+// Work schedule shared by every warp role (each role walks the same segments in the same order).
+// ------------------------------------------------------------------------------------------------
+struct Sched {
+    int64_t tiles;     // weight tiles * activation tiles
+    int tiles_m;       // activation-row tiles
+    int kbt;           // k-blocks per tile
+    int G;             // CTAs
+    int sk;            // 1 = stream-K, 0 = whole tiles
+};
+
+struct Seg {
+    int64_t tile;
+    int kb_lo, kb_hi;
+};
+
+struct SegState {
+    int64_t next;      // SK: next iteration; DP: next tile
+    int64_t end;       // SK: end iteration
+};
+
+__device__ __forceinline__ int64_t sk_start(const Sched& s, int c) {
+    return (int64_t)c * (s.tiles * s.kbt) / s.G;
+}
+
+__device__ __forceinline__ void seg_init(const Sched& s, int c, SegState& st) {
+    if (s.sk) {
+        st.next = sk_start(s, c);
+        st.end = sk_start(s, c + 1);
+    } else {
+        st.next = c;
+        st.end = s.tiles;
+    }
+}
+
+__device__ __forceinline__ bool seg_next(const Sched& s, SegState& st, Seg& g) {
+    if (st.next >= st.end) return false;
+    if (s.sk) {
+        g.tile = st.next / s.kbt;
+        g.kb_lo = (int)(st.next % s.kbt);
+        const int64_t left = st.end - st.next;
+        g.kb_hi = left < (int64_t)(s.kbt - g.kb_lo) ? g.kb_lo + (int)left : s.kbt;
+        st.next += g.kb_hi - g.kb_lo;
+    } else {
+        g.tile = st.next;
+        g.kb_lo = 0;
+        g.kb_hi = s.kbt;
+        st.next += s.G;
+    }
+    return true;
+}
+
+__device__ __forceinline__ uint32_t ld_acquire(const uint32_t* p) {
+    uint32_t v;
+    asm volatile("ld.acquire.gpu.global.u32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
+    return v;
+}
+__device__ __forceinline__ void st_release(uint32_t* p, uint32_t v) {
+    asm volatile("st.release.gpu.global.u32 [%0], %1;" :: "l"(p), "r"(v) : "memory");
+}
+__device__ __forceinline__ void epi_bar() {  // the 4 epilogue warps only
+    asm volatile("bar.sync 1, %0;" :: "n"(EPI_THREADS) : "memory");
+}
+
+// 16 columns of 32-bit accumulators: thread i of the warp gets lane (taddr.lane + i).
+__device__ __forceinline__ void tmem_ld16(uint32_t taddr, uint32_t (&v)[16]) {
+    asm volatile(
+        "tcgen05.ld.sync.aligned.32x32b.x16.b32 "
+        "{%0,%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15}, [%16];"
+        : "=r"(v[0]), "=r"(v[1]), "=r"(v[2]), "=r"(v[3]), "=r"(v[4]), "=r"(v[5]), "=r"(v[6]), "=r"(v[7]),
+          "=r"(v[8]), "=r"(v[9]), "=r"(v[10]), "=r"(v[11]), "=r"(v[12]), "=r"(v[13]), "=r"(v[14]), "=r"(v[15])
+        : "r"(taddr));
+}
+
+// Per-thread dequantizer of one weight row's super-blocks (256 k-elements = 4 k-blocks). The thread
+// owns half of every k-block (PART 0/1) and writes it, rounded to bf16/f16, into the row's 128-byte
+// swizzled line of the operand tile. Everything a super-block needs beyond the raw TMA stage (block
+// scales kept in global memory) is loaded one super-block ahead (prefetch) so no global load sits
+// on the critical path; Q4_K's header is decoded once per super-block into 8 (d*sc, dmin*m) pairs.
+//   Q4_K part p: qs bytes 32j + 16p .. +16 -> low-nibble chunks 2p, 2p+1 and high-nibble chunks
+//                2p+4, 2p+5 of k-block j (sub-blocks 2j and 2j+1)
+//   others part p: chunks 4p .. 4p+3 of k-block j
+template <bool BF16>
+__device__ __forceinline__ void store_chunk8(uint8_t* arow, int sw, int c, const float (&v)[8]) {
+    uint4 pk;
+    pk.x = pack2<BF16>(v[0], v[1]);
+    pk.y = pack2<BF16>(v[2], v[3]);
+    pk.z = pack2<BF16>(v[4], v[5]);
+    pk.w = pack2<BF16>(v[6], v[7]);
+    *reinterpret_cast<uint4*>(arow + 16 * (c ^ sw)) = pk;
+}
+
+// 8 exact values (d*sc)*q - dmin*m (as fma, see jk_decode.cuh) of the 4 nibble-bytes of w0, w1
+__device__ __forceinline__ void q4k_vals(uint32_t w0, uint32_t w1, float dd, float mm, float (&v)[8]) {
+    const uint32_t ws[2] = {w0, w1};
+#pragma unroll
+    for (int t = 0; t < 2; ++t)
+#pragma unroll
+        for (int i = 0; i < 4; i += 2) {
+            const float2 q = sub2(make_float2(magic_byte(ws[t], i), magic_byte(ws[t], i + 1)), make_float2(MAGIC, MAGIC));
+            const float2 r = fma2(make_float2(dd, dd), q, make_float2(-mm, -mm));
+            v[4 * t + i] = r.x;
+            v[4 * t + i + 1] = r.y;
+        }
+}
+
+template <int FMT, bool BF16, int PART>
+struct SbDequant;
+
+template <bool BF16, int PART>
+struct SbDequant<FMT_Q4K, BF16, PART> {
+    float dd[8], mm[8];
+    __device__ __forceinline__ void prefetch(const WView&, int64_t, int) {}
+    __device__ __forceinline__ void begin(const uint8_t* raw_row, const WView&, int64_t, bool, int) {
+        const uint4 hdr = *reinterpret_cast<const uint4*>(raw_row);
+        const float d = half_bits_to_float(hdr.x & 0xFFFFu);
+        const float dmin = half_bits_to_float(hdr.x >> 16);
+#pragma unroll
+        for (int j = 0; j < 8; ++j) {
+            uint32_t sc, mn;
+            q4k_scale_min(hdr.y, hdr.z, hdr.w, j, sc, mn);  // j is a compile-time constant here
+            dd[j] = __fmul_rn(d, (float)sc);
+            mm[j] = __fmul_rn(dmin, (float)mn);
+        }
+    }
+    template <int J>
+    __device__ __forceinline__ void kblock(const uint8_t* raw_row, int, uint8_t* arow, int sw) {
+        const uint4 q = *reinterpret_cast<const uint4*>(raw_row + 16 + 32 * J + 16 * PART);
+        float v[8];
+        q4k_vals(q.x & 0x0F0F0F0Fu, q.y & 0x0F0F0F0Fu, dd[2 * J], mm[2 * J], v);
+        store_chunk8<BF16>(arow, sw, 2 * PART, v);
+        q4k_vals(q.z & 0x0F0F0F0Fu, q.w & 0x0F0F0F0Fu, dd[2 * J], mm[2 * J], v);
+        store_chunk8<BF16>(arow, sw, 2 * PART + 1, v);
+        q4k_vals((q.x >> 4) & 0x0F0F0F0Fu, (q.y >> 4) & 0x0F0F0F0Fu, dd[2 * J + 1], mm[2 * J + 1], v);
+        store_chunk8<BF16>(arow, sw, 2 * PART + 4, v);
+        q4k_vals((q.z >> 4) & 0x0F0F0F0Fu, (q.w >> 4) & 0x0F0F0F0Fu, dd[2 * J + 1], mm[2 * J + 1], v);
+        store_chunk8<BF16>(arow, sw, 2 * PART + 5, v);
+    }
+};
+
+template <bool BF16, int PART>
+struct SbDequant<FMT_Q6K, BF16, PART> {
+    uint32_t d_next = 0;
+    float d = 0.f;
+    __device__ __forceinline__ void prefetch(const WView& w, int64_t rr, int sb) {
+        d_next = __ldg(w.d + rr * (w.k / 256) + sb);
+    }
+    __device__ __forceinline__ void begin(const uint8_t*, const WView&, int64_t, bool row_ok, int) {
+        d = row_ok ? half_bits_to_float(d_next) : 0.f;
+    }
+    template <int J>
+    __device__ __forceinline__ void kblock(const uint8_t* body, int, uint8_t* arow, int sw) {
+        Q6KBlock bq;
+        bq.load(body, d, J);
+        float v[8];
+#pragma unroll
+        for (int i = 0; i < 4; ++i) {
+            bq.chunk(4 * PART + i, v);
+            store_chunk8<BF16>(arow, sw, 4 * PART + i, v);
+        }
+    }
+};
+
+template <bool BF16, int PART>
+struct SbDequant<FMT_Q8_0, BF16, PART> {
+    uint4 d_next = make_uint4(0, 0, 0, 0);  // f16 scales of the super-block's 8 blocks
+    uint4 dcur = make_uint4(0, 0, 0, 0);
+    __device__ __forceinline__ void prefetch(const WView& w, int64_t rr, int sb) {
+        const uint16_t* p = w.d + rr * (w.k / 32) + 8 * sb;
+        if ((w.k & 255) == 0) {
+            d_next = __ldg(reinterpret_cast<const uint4*>(p));
+        } else {  // row not 16-byte aligned or partial super-block: load the valid pairs
+            uint32_t t[4] = {0u, 0u, 0u, 0u};
+            const int64_t nb = w.k / 32 - 8 * (int64_t)sb;
+            for (int i = 0; i < 4; ++i)
+                if (2 * i < nb) t[i] = __ldg(reinterpret_cast<const uint32_t*>(p) + i);
+            d_next = make_uint4(t[0], t[1], t[2], t[3]);
+        }
+    }
+    __device__ __forceinline__ void begin(const uint8_t*, const WView&, int64_t, bool row_ok, int) {
+        dcur = row_ok ? d_next : make_uint4(0, 0, 0, 0);
+    }
+    template <int J>
+    __device__ __forceinline__ void kblock(const uint8_t* raw_row_half0, int row, uint8_t* arow, int sw) {
+        // k-block J: 128-byte swizzled half J/2 of the stage (the caller points raw_row_half0 at
+        // half 0's row; half 1 starts BW * 128 bytes later), logical chunks 4 (J%2) ..
+        const uint32_t dw = (J >> 1) == 0 ? ((J & 1) ? dcur.y : dcur.x) : ((J & 1) ? dcur.w : dcur.z);
+        Q80Block bq;
+        bq.load_sw(raw_row_half0 + (J >> 1) * (BW * 128), 4 * (J & 1), row, half_bits_to_float(dw & 0xFFFFu),
+                   half_bits_to_float(dw >> 16));
+        float v[8];
+#pragma unroll
+        for (int i = 0; i < 4; ++i) {
+            bq.chunk(4 * PART + i, v);
+            store_chunk8<BF16>(arow, sw, 4 * PART + i, v);
+        }
+    }
+};
+
+template <bool BF16, int PART>
+struct SbDequant<FMT_Q5_0, BF16, PART> {
+    uint4 d_next = make_uint4(0, 0, 0, 0), h_next0 = make_uint4(0, 0, 0, 0), h_next1 = make_uint4(0, 0, 0, 0);
+    uint4 dcur = make_uint4(0, 0, 0, 0), h0 = make_uint4(0, 0, 0, 0), h1 = make_uint4(0, 0, 0, 0);
+    __device__ __forceinline__ void prefetch(const WView& w, int64_t rr, int sb) {
+        const int64_t nb = w.k / 32 - 8 * (int64_t)sb;
+        const uint16_t* pd = w.d + rr * (w.k / 32) + 8 * sb;
+        const uint32_t* ph = w.h + rr * (w.k / 32) + 8 * sb;
+        uint32_t t[4] = {0u, 0u, 0u, 0u}, a[8] = {0u, 0u, 0u, 0u, 0u, 0u, 0u, 0u};
+        for (int i = 0; i < 4; ++i)
+            if (2 * i < nb) t[i] = __ldg(reinterpret_cast<const uint32_t*>(pd) + i);
+        for (int i = 0; i < 8; ++i)
+            if (i < nb) a[i] = __ldg(ph + i);
+        d_next = make_uint4(t[0], t[1], t[2], t[3]);
+        h_next0 = make_uint4(a[0], a[1], a[2], a[3]);
+        h_next1 = make_uint4(a[4], a[5], a[6], a[7]);
+    }
+    __device__ __forceinline__ void begin(const uint8_t*, const WView&, int64_t, bool row_ok, int) {
+        dcur = row_ok ? d_next : make_uint4(0, 0, 0, 0);
+        h0 = h_next0;
+        h1 = h_next1;
+    }
+    template <int J>
+    __device__ __forceinline__ void kblock(const uint8_t* rowp, int, uint8_t* arow, int sw) {
+        // 128-byte swizzled row of the super-block; k-block J = logical chunks 2J, 2J+1
+        const uint32_t dw = (J >> 1) == 0 ? ((J & 1) ? dcur.y : dcur.x) : ((J & 1) ? dcur.w : dcur.z);
+        const uint32_t ha = J == 0 ? h0.x : J == 1 ? h0.z : J == 2 ? h1.x : h1.z;
+        const uint32_t hb = J == 0 ? h0.y : J == 1 ? h0.w : J == 2 ? h1.y : h1.w;
+        Q50Block bq;
+        bq.load_words(*reinterpret_cast<const uint4*>(rowp + 16 * ((2 * J) ^ sw)),
+                      *reinterpret_cast<const uint4*>(rowp + 16 * ((2 * J + 1) ^ sw)), ha, hb,
+                      half_bits_to_float(dw & 0xFFFFu), half_bits_to_float(dw >> 16));
+        float v[8];
+#pragma unroll
+        for (int i = 0; i < 4; ++i) {
+            bq.chunk(4 * PART + i, v);
+            store_chunk8<BF16>(arow, sw, 4 * PART + i, v);
+        }
+    }
+};
+
+template <int FMT, bool BF16, int BT, int PART>
+__device__ __forceinline__ void dequant_role(const Sched& sched, SegState& ss, uint8_t* smem, int row_in_tile,
+                                             const WView& w, uint32_t* err, bool& ok, uint32_t bar0, int lane) {
+    using L = Smem<FMT, BT>;
+    constexpr int S = L::S, R = L::R;
+    auto full_a = [&](int s) { return bar0 + 8u * (S + s); };
+    auto empty = [&](int s) { return bar0 + 8u * (2 * S + s); };
+    auto raw_full = [&](int r) { return bar0 + 8u * (3 * S + r); };
+    auto raw_empty = [&](int r) { return bar0 + 8u * (3 * S + R + r); };
+    const int sw = row_in_tile & 7;
+    SbDequant<FMT, BF16, PART> dq;
+    int it = 0, raw_n = 0;
+    Seg sg;
+    while (ok && seg_next(sched, ss, sg)) {
+        const int64_t row = (sg.tile / sched.tiles_m) * BW + row_in_tile;
+        const bool row_ok = row < w.rows;
+        const int64_t rr = row_ok ? row : 0;
+        const int sb_lo = sg.kb_lo >> 2, sb_hi = (sg.kb_hi - 1) >> 2;
+        dq.prefetch(w, rr, sb_lo);
+        for (int sb = sb_lo; sb <= sb_hi && ok; ++sb) {
+            const int r = raw_n++;
+            const int slot = r % R;
+            ok = __all_sync(0xFFFFFFFFu, mbar_wait(raw_full(slot), (r / R) & 1, err));
+            if (!ok) break;
+            const uint8_t* raw = smem + L::off_raw + slot * L::raw_bytes;
+            const uint8_t* raw_row = raw + row_in_tile * (FMT == FMT_Q4K ? 144 : FMT == FMT_Q6K ? 208 : 128);
+            dq.begin(raw_row, w, rr, row_ok, sb);
+            if (sb < sb_hi) dq.prefetch(w, rr, sb + 1);
+#pragma unroll
+            for (int j = 0; j < 4; ++j) {
+                const int kb = 4 * sb + j;
+                if (kb < sg.kb_lo || kb >= sg.kb_hi) continue;
+                const int s = it % S;
+                if (it >= S) ok = __all_sync(0xFFFFFFFFu, mbar_wait(empty(s), ((it / S) - 1) & 1, err));
+                if (!ok) break;
+                JK_TRACE_POINT(6, it);
+                uint8_t* arow = smem + L::off_a + s * A_STAGE_BYTES + row_in_tile * 128;
+                switch (j) {
+                case 0: dq.template kblock<0>(raw_row, row_in_tile, arow, sw); break;
+                case 1: dq.template kblock<1>(raw_row, row_in_tile, arow, sw); break;
+                case 2: dq.template kblock<2>(raw_row, row_in_tile, arow, sw); break;
+                default: dq.template kblock<3>(raw_row, row_in_tile, arow, sw); break;
+                }
+                fence_proxy_async_smem();
+                __syncwarp();
+                JK_TRACE_POINT(9, it);
+                if (lane == 0) mbar_arrive(full_a(s));
+                ++it;
+            }
+            if (!ok) break;
+            __syncwarp();
+            if (lane == 0) mbar_arrive(raw_empty(slot));
+        }
+    }
 }
 
 template <int FMT, bool BF16, int BT>
 __global__ void __launch_bounds__(THREADS, 1)
 gemm_tc_kernel(const __grid_constant__ CUtensorMap tm_x, const __grid_constant__ CUtensorMap tm_w, WView w,
-               float* __restrict__ out, int64_t m, int64_t ldo, int64_t part_stride, int kb_total, int splits,
-               uint32_t* err) {
+               float* __restrict__ out, int64_t m, int64_t ldo, Sched sched, float* __restrict__ ws_part,
+               uint32_t* __restrict__ ws_flag, uint32_t* err) {
     using L = Smem<FMT, BT>;
     constexpr int S = L::S;
     constexpr bool QUANT = FMT != FMT_F16;
-    constexpr uint32_t TMEM_COLS = BT < 32 ? 32 : BT;
+    constexpr uint32_t TMEM_COLS = 2 * BT;
     constexpr uint32_t IDESC = idesc_f16(BF16, BW, BT);
 
     extern __shared__ uint8_t smem_raw[];
@@ -98,36 +392,34 @@ gemm_tc_kernel(const __grid_constant__ CUtensorMap tm_x, const __grid_constant__
     auto full_b = [&](int s) { return bar0 + 8u * s; };
     auto full_a = [&](int s) { return bar0 + 8u * (S + s); };
     auto empty = [&](int s) { return bar0 + 8u * (2 * S + s); };
+    constexpr int R = L::R;
     auto raw_full = [&](int r) { return bar0 + 8u * (3 * S + r); };
-    auto raw_empty = [&](int r) { return bar0 + 8u * (3 * S + 2 + r); };
-    const uint32_t acc_full = bar0 + 8u * (3 * S + 4);
+    auto raw_empty = [&](int r) { return bar0 + 8u * (3 * S + R + r); };
+    auto acc_full = [&](int b) { return bar0 + 8u * (3 * S + 2 * R + b); };
+    auto acc_empty = [&](int b) { return bar0 + 8u * (3 * S + 2 * R + 2 + b); };
     uint32_t* tmem_holder = reinterpret_cast<uint32_t*>(smem + L::off_tmem);
 
     const int warp = threadIdx.x >> 5;
     const int lane = threadIdx.x & 31;
-
-    const int64_t n0 = (int64_t)blockIdx.x * BW;   // first weight row of the tile
-    const int64_t m0 = (int64_t)blockIdx.y * BT;   // first activation row
-    const int z = blockIdx.z;
-    const int kb_begin = (int)((int64_t)z * kb_total / splits);
-    const int kb_end = (int)((int64_t)(z + 1) * kb_total / splits);
-    const int nkb = kb_end - kb_begin;
-    const int sb_begin = kb_begin / 4;
+    const int cta = blockIdx.x;
 
     if (threadIdx.x == 0) {
         for (int s = 0; s < S; ++s) {
             mbar_init(full_b(s), 1);
-            mbar_init(full_a(s), 4);
+            mbar_init(full_a(s), DQ_WARPS);
             mbar_init(empty(s), 1);
         }
-        for (int r = 0; r < 2; ++r) {
+        for (int r = 0; r < R; ++r) {
             mbar_init(raw_full(r), 1);
-            mbar_init(raw_empty(r), 4);
+            mbar_init(raw_empty(r), DQ_WARPS);
         }
-        mbar_init(acc_full, 1);
+        for (int b = 0; b < 2; ++b) {
+            mbar_init(acc_full(b), 1);
+            mbar_init(acc_empty(b), EPI_WARPS);
+        }
         mbar_fence_init();
     }
-    if (warp == 1) {
+    if (warp == MMA_WARP) {
         tmem_alloc(smem_u32(tmem_holder), TMEM_COLS);
         tmem_relinquish();
     }
@@ -136,243 +428,306 @@ gemm_tc_kernel(const __grid_constant__ CUtensorMap tm_x, const __grid_constant__
     tc_fence_after();
     const uint32_t tmem = *tmem_holder;
 
-    bool ok = nkb > 0;
+    bool ok = true;
+    SegState ss;
+    seg_init(sched, cta, ss);
+    Seg sg;
 
-    if (warp == 0) {
-        if (lane == 0 && ok) {
-            // ---------------- producer ----------------
+    // The producer, raw-producer and MMA roles run their loops with the whole warp converged (waits
+    // on every lane, warp-uniform addresses and descriptors); one lane issues the TMA copies, the
+    // MMAs and the commits.
+    const bool leader = lane == 0;
+    if (warp == PRODUCER_WARP) {
+        // --------------------- activation (and FP16 weight) producer ---------------------
+        if (leader) {
             tma_prefetch(&tm_x);
-            if (QUANT || FMT == FMT_F16) tma_prefetch(&tm_w);
-            int last_raw = -1;
-            int issued = 0;      // operand stages whose copies were issued
-            int raw_issued = 0;  // raw weight stages whose copies were issued
-            for (int it = 0; it < nkb && ok; ++it) {
-                const int kb = kb_begin + it;
+            tma_prefetch(&tm_w);
+        }
+        int it = 0;
+        while (ok && seg_next(sched, ss, sg)) {
+            const int32_t n0 = (int32_t)((sg.tile / sched.tiles_m) * BW);
+            const int32_t m0 = (int32_t)((sg.tile % sched.tiles_m) * BT);
+            for (int kb = sg.kb_lo; kb < sg.kb_hi && ok; ++kb) {
                 const int s = it % S;
-                if constexpr (QUANT) {
+                if (it >= S) ok = __all_sync(0xFFFFFFFFu, mbar_wait(empty(s), ((it / S) - 1) & 1, err));
+                if (!ok) break;
+                JK_TRACE_POINT(1, it);
+                if (leader) {
+                    if constexpr (FMT == FMT_F16) {
+                        mbar_expect_tx(full_b(s), L::B_STAGE + A_STAGE_BYTES);
+                        tma_load_2d(sbase + L::off_a + s * A_STAGE_BYTES, &tm_w, kb * KB, n0, full_b(s));
+                    } else {
+                        mbar_expect_tx(full_b(s), L::B_STAGE);
+                    }
+                    tma_load_2d(sbase + L::off_b + s * L::B_STAGE, &tm_x, kb * KB, m0, full_b(s));
+                }
+                __syncwarp();
+                ++it;
+            }
+        }
+        if (!ok)  // drain: every copy this warp issued lands before the CTA may exit
+            for (int i = it - S < 0 ? 0 : it - S; i < it; ++i) mbar_wait(full_b(i % S), (i / S) & 1, err);
+    } else if (warp == RAW_WARP) {
+        // --------------------- raw weight producer: runs up to R super-blocks ahead ---------------------
+        if constexpr (QUANT) {
+            int raw_n = 0;
+            while (ok && seg_next(sched, ss, sg)) {
+                const int32_t n0 = (int32_t)((sg.tile / sched.tiles_m) * BW);
+                for (int kb = sg.kb_lo; kb < sg.kb_hi && ok; ++kb) {
+                    if (kb != sg.kb_lo && (kb & 3) != 0) continue;
+                    const int r = raw_n;
+                    const int slot = r % R;
+                    if (r >= R) ok = __all_sync(0xFFFFFFFFu, mbar_wait(raw_empty(slot), ((r / R) - 1) & 1, err));
+                    if (!ok) break;
+                    ++raw_n;
+                    JK_TRACE_POINT(2, r);
                     const int sb = kb >> 2;
-                    if (sb != last_raw) {
-                        const int r = sb - sb_begin;
-                        const int slot = r & 1;
-                        if (r >= 2) ok = mbar_wait(raw_empty(slot), ((r >> 1) - 1) & 1, err);
-                        if (!ok) break;
-                        const uint32_t dst = sbase + L::off_raw + slot * L::raw_bytes;
+                    const uint32_t dst = sbase + L::off_raw + slot * L::raw_bytes;
+                    if (leader) {
                         mbar_expect_tx(raw_full(slot), L::raw_bytes);
                         if constexpr (FMT == FMT_Q4K) {
-                            tma_load_2d(dst, &tm_w, sb * 36, (int32_t)n0, raw_full(slot));
+                            tma_load_2d(dst, &tm_w, sb * 36, n0, raw_full(slot));
                         } else if constexpr (FMT == FMT_Q6K) {
-                            tma_load_2d(dst, &tm_w, sb * 52, (int32_t)n0, raw_full(slot));
+                            tma_load_2d(dst, &tm_w, sb * 52, n0, raw_full(slot));
                         } else if constexpr (FMT == FMT_Q8_0) {
-                            tma_load_2d(dst, &tm_w, sb * 256, (int32_t)n0, raw_full(slot));
-                            tma_load_2d(dst + BW * 128, &tm_w, sb * 256 + 128, (int32_t)n0, raw_full(slot));
-                        } else {  // Q5_0
-                            tma_load_2d(dst, &tm_w, sb * 128, (int32_t)n0, raw_full(slot));
+                            tma_load_2d(dst, &tm_w, sb * 256, n0, raw_full(slot));
+                            tma_load_2d(dst + BW * 128, &tm_w, sb * 256 + 128, n0, raw_full(slot));
+                        } else {
+                            tma_load_2d(dst, &tm_w, sb * 128, n0, raw_full(slot));
                         }
-                        last_raw = sb;
-                        raw_issued = r + 1;
                     }
+                    __syncwarp();
                 }
-                if (it >= S) ok = mbar_wait(empty(s), ((it / S) - 1) & 1, err);
-                if (!ok) break;
-                const uint32_t b_dst = sbase + L::off_b + s * L::B_STAGE;
-                if constexpr (FMT == FMT_F16) {
-                    mbar_expect_tx(full_b(s), L::B_STAGE + A_STAGE_BYTES);
-                    tma_load_2d(sbase + L::off_a + s * A_STAGE_BYTES, &tm_w, kb * KB, (int32_t)n0, full_b(s));
-                } else {
-                    mbar_expect_tx(full_b(s), L::B_STAGE);
-                }
-                tma_load_2d(b_dst, &tm_x, kb * KB, (int32_t)m0, full_b(s));
-                issued = it + 1;
             }
-            // Error path: wait (bounded) until the copies issued last have landed before leaving,
-            // so no copy writes this CTA's shared memory after it exits.
-            if (!ok) {
-                for (int it = issued - S < 0 ? 0 : issued - S; it < issued; ++it)
-                    mbar_wait(full_b(it % S), (it / S) & 1, err);
-                for (int r = raw_issued - 2 < 0 ? 0 : raw_issued - 2; r < raw_issued; ++r)
-                    mbar_wait(raw_full(r & 1), (r >> 1) & 1, err);
-            }
+            if (!ok)
+                for (int r = raw_n - R < 0 ? 0 : raw_n - R; r < raw_n; ++r) mbar_wait(raw_full(r % R), (r / R) & 1, err);
         }
-    } else if (warp == 1) {
-        if (lane == 0) {
-            // ---------------- MMA issuer ----------------
-            if (ok) {
-                for (int it = 0; it < nkb; ++it) {
-                    const int s = it % S;
-                    const uint32_t ph = (it / S) & 1;
-                    ok = mbar_wait(full_b(s), ph, err);
-                    if (ok && QUANT) ok = mbar_wait(full_a(s), ph, err);
-                    if (!ok) break;
-                    tc_fence_after();
-                    const uint64_t ad = sw128_kmajor_desc(sbase + L::off_a + s * A_STAGE_BYTES);
-                    const uint64_t bd = sw128_kmajor_desc(sbase + L::off_b + s * L::B_STAGE);
+    } else if (warp == MMA_WARP) {
+        // ------------------------------ MMA issuer ------------------------------
+        int it = 0, seg_i = 0;
+        bool issued = false;
+        while (ok && seg_next(sched, ss, sg)) {
+            const int b = seg_i & 1;
+            if (seg_i >= 2) ok = __all_sync(0xFFFFFFFFu, mbar_wait(acc_empty(b), ((seg_i >> 1) - 1) & 1, err));
+            if (!ok) break;
+            tc_fence_after();
+            const uint32_t acc = tmem + (uint32_t)(b * BT);
+            for (int kb = sg.kb_lo; kb < sg.kb_hi; ++kb, ++it) {
+                const int s = it % S;
+                const uint32_t ph = (it / S) & 1;
+                bool got = mbar_wait(full_b(s), ph, err);
+                JK_TRACE_POINT(3, it);
+                if (got && QUANT) got = mbar_wait(full_a(s), ph, err);
+                ok = __all_sync(0xFFFFFFFFu, got);
+                if (!ok) break;
+                JK_TRACE_POINT(4, it);
+                tc_fence_after();
+                const uint64_t ad = sw128_kmajor_desc(sbase + L::off_a + s * A_STAGE_BYTES);
+                const uint64_t bd = sw128_kmajor_desc(sbase + L::off_b + s * L::B_STAGE);
+                if (leader) {
 #pragma unroll
-                    for (int k = 0; k < KB / 16; ++k) {
-                        // +32 bytes per K=16 step inside the 128-byte swizzle atom (>>4 => +2)
-                        mma_f16(tmem, ad + 2u * k, bd + 2u * k, IDESC, (it > 0 || k > 0) ? 1u : 0u);
-                    }
+                    for (int k = 0; k < KB / 16; ++k)  // +32 bytes per K=16 step inside the swizzle atom
+                        mma_f16(acc, ad + 2u * k, bd + 2u * k, IDESC, (kb > sg.kb_lo || k > 0) ? 1u : 0u);
                     mma_commit(empty(s));
                 }
-            }
-            // Signals the epilogue (and, on the error path, lets this thread drain its MMAs).
-            mma_commit(acc_full);
-            if (!ok) mbar_wait(acc_full, 0, err);
-        }
-    } else {
-        // ---------------- dequantizers, then epilogue ----------------
-        const int t = threadIdx.x - 64;      // 0..127: weight row within the tile
-        const int quarter = warp & 3;        // TMEM lane quarter this warp may access
-        if constexpr (QUANT) {
-            const int64_t row = n0 + t;
-            const bool row_ok = row < w.rows;
-            const int64_t rr = row_ok ? row : 0;
-            for (int it = 0; it < nkb && ok; ++it) {
-                const int kb = kb_begin + it;
-                const int s = it % S;
-                const int sb = kb >> 2;
-                const int r = sb - sb_begin;
-                const int slot = r & 1;
-                ok = mbar_wait(raw_full(slot), (r >> 1) & 1, err);
-                if (ok && it >= S) ok = mbar_wait(empty(s), ((it / S) - 1) & 1, err);
-                ok = __all_sync(0xFFFFFFFFu, ok);  // keep the warp converged on every path
-                if (!ok) break;
-                const uint8_t* raw = smem + L::off_raw + slot * L::raw_bytes;
-                uint8_t* arow = smem + L::off_a + s * A_STAGE_BYTES + t * 128;
-                const int j = kb & 3;
-                float v[8];
-                auto store_chunk = [&](int c) {
-                    const float (&vv)[8] = v;
-                    uint4 pk;
-                    pk.x = pack2<BF16>(vv[0], vv[1]);
-                    pk.y = pack2<BF16>(vv[2], vv[3]);
-                    pk.z = pack2<BF16>(vv[4], vv[5]);
-                    pk.w = pack2<BF16>(vv[6], vv[7]);
-                    *reinterpret_cast<uint4*>(arow + 16 * (c ^ (t & 7))) = pk;
-                };
-                if constexpr (FMT == FMT_Q4K) {
-                    Q4KBlock b;
-                    b.load(raw + t * 144, j);
-#pragma unroll
-                    for (int c = 0; c < 8; ++c) { b.chunk(c, v); store_chunk(c); }
-                } else if constexpr (FMT == FMT_Q6K) {
-                    Q6KBlock b;
-                    const float d = row_ok ? half_bits_to_float(__ldg(w.d + rr * (w.k / 256) + sb)) : 0.f;
-                    b.load(raw + t * 208, d, j);
-#pragma unroll
-                    for (int c = 0; c < 8; ++c) { b.chunk(c, v); store_chunk(c); }
-                } else if constexpr (FMT == FMT_Q8_0) {
-                    Q80Block b;
-                    float d0 = 0.f, d1 = 0.f;
-                    if (row_ok) {
-                        const uint32_t dw = __ldg(reinterpret_cast<const uint32_t*>(w.d + rr * (w.k / 32) + 2 * kb));
-                        d0 = half_bits_to_float(dw & 0xFFFFu);
-                        d1 = half_bits_to_float(dw >> 16);
-                    }
-                    // k-block j of the super-block: 128-byte swizzled half (j/2), chunks 4(j%2)..
-                    b.load_sw(raw + (j >> 1) * (BW * 128) + t * 128, 4 * (j & 1), t, d0, d1);
-#pragma unroll
-                    for (int c = 0; c < 8; ++c) { b.chunk(c, v); store_chunk(c); }
-                } else {  // Q5_0
-                    Q50Block b;
-                    float d0 = 0.f, d1 = 0.f;
-                    uint32_t qh2[2] = {0u, 0u};
-                    if (row_ok) {
-                        const uint32_t dw = __ldg(reinterpret_cast<const uint32_t*>(w.d + rr * (w.k / 32) + 2 * kb));
-                        d0 = half_bits_to_float(dw & 0xFFFFu);
-                        d1 = half_bits_to_float(dw >> 16);
-                        qh2[0] = __ldg(w.h + rr * (w.k / 32) + 2 * kb);
-                        qh2[1] = __ldg(w.h + rr * (w.k / 32) + 2 * kb + 1);
-                    }
-                    // 128-byte swizzled row of the super-block; k-block j = chunks 2j, 2j+1
-                    uint8_t tmp[32];
-                    const uint8_t* rowp = raw + t * 128;
-                    *reinterpret_cast<uint4*>(tmp) = *reinterpret_cast<const uint4*>(rowp + 16 * ((2 * j) ^ (t & 7)));
-                    *reinterpret_cast<uint4*>(tmp + 16) = *reinterpret_cast<const uint4*>(rowp + 16 * ((2 * j + 1) ^ (t & 7)));
-                    b.load(tmp, qh2, d0, d1);
-#pragma unroll
-                    for (int c = 0; c < 8; ++c) { b.chunk(c, v); store_chunk(c); }
-                }
-                fence_proxy_async_smem();
                 __syncwarp();
-                if (lane == 0) {
-                    mbar_arrive(full_a(s));
-                    if (j == 3 || it == nkb - 1) mbar_arrive(raw_empty(slot));
-                }
+                issued = true;
             }
+            if (!ok) break;
+            if (leader) mma_commit(acc_full(b));  // arrives when this segment's MMAs are complete
+            __syncwarp();
+            ++seg_i;
         }
-        // ---------------- epilogue ----------------
-        if (nkb > 0) {
-            const bool acc_ok = __all_sync(0xFFFFFFFFu, mbar_wait(acc_full, 0, err) && ok);
+        if (!ok && issued) {
+            // Error path: drain the MMAs issued so far before TMEM is released. The commit arrives on
+            // acc_full(b) of the unfinished segment; wait for it.
+            const int b = seg_i & 1;
+            if (leader) mma_commit(acc_full(b));
+            __syncwarp();
+            mbar_wait(acc_full(b), (seg_i >> 1) & 1, err);
+        }
+    } else if (warp < DQ_WARP0) {
+        // ------------------------------ epilogue ------------------------------
+        const int quarter = warp & 3;                 // TMEM lanes this warp may read
+        const int row_in_tile = 32 * quarter + lane;  // weight row within the tile
+        int seg_i = 0;
+        while (ok && seg_next(sched, ss, sg)) {
+            const int b = seg_i & 1;
+            ok = __all_sync(0xFFFFFFFFu, mbar_wait_sleepy(acc_full(b), (seg_i >> 1) & 1, err));
             tc_fence_after();
-            if (acc_ok) {
-                const int64_t wrow = n0 + 32 * quarter + lane;
-                float* obase = out + (int64_t)z * part_stride;
+            if (!ok) break;
+            JK_TRACE_POINT(7, seg_i);
+            const int64_t n0 = (sg.tile / sched.tiles_m) * BW;
+            const int64_t m0 = (sg.tile % sched.tiles_m) * BT;
+            const int64_t wrow = n0 + row_in_tile;
+            const bool contributor = sg.kb_lo > 0;
+            const bool owner = sg.kb_lo == 0 && sg.kb_hi < sched.kbt;
+            // contributors of an owned tile: the following CTAs whose ranges start inside it
+            int c_last = cta;
+            if (owner) {
+                const int64_t tile_end = (sg.tile + 1) * sched.kbt;
+                while (c_last + 1 < sched.G && sk_start(sched, c_last + 1) < tile_end) ++c_last;
+                __shared__ int flags_ok;
+                if (threadIdx.x == 32 * EPI_WARP0) {
+                    bool good = true;
+                    for (int c = cta + 1; c <= c_last && good; ++c) {
+                        const uint64_t t0 = globaltimer();
+                        while (ld_acquire(ws_flag + c) == 0u) {
+                            if (globaltimer() - t0 > WAIT_LIMIT_NS) {
+                                atomicOr(err, ERR_WAIT_TIMEOUT);
+                                good = false;
+                                break;
+                            }
+                        }
+                    }
+                    flags_ok = good ? 1 : 0;
+                }
+                epi_bar();
+                ok = flags_ok != 0;
+            }
+            if (ok) {
+                const uint32_t tbase = tmem + ((uint32_t)(32 * quarter) << 16) + (uint32_t)(b * BT);
+                // CH columns per round: all TMEM loads of the round are issued before one wait, and an
+                // owner loads all contributor partials of the round before adding them.
+                constexpr int CH = BT < 64 ? BT : 64;
 #pragma unroll 1
-                for (int cc = 0; cc < BT / 32; ++cc) {
-                    uint32_t v[32];
-                    tmem_ld32(tmem + ((uint32_t)(32 * quarter) << 16) + 32u * cc, v);
-                    tmem_ld_wait();
-                    if (wrow < w.rows) {
+                for (int c0 = 0; c0 < BT; c0 += CH) {
+                    uint32_t v[CH];
 #pragma unroll
-                        for (int jj = 0; jj < 32; ++jj) {
-                            const int64_t mr = m0 + 32 * cc + jj;
-                            if (mr < m) obase[mr * ldo + wrow] = __uint_as_float(v[jj]);
+                    for (int q = 0; q < CH / 16; ++q) {
+                        uint32_t (&vq)[16] = *reinterpret_cast<uint32_t(*)[16]>(&v[16 * q]);
+                        tmem_ld16(tbase + (uint32_t)(c0 + 16 * q), vq);
+                    }
+                    tmem_ld_wait();
+                    if (contributor) {
+                        float* slot = ws_part + (int64_t)cta * BT * BW + (int64_t)c0 * BW + row_in_tile;
+#pragma unroll
+                        for (int j = 0; j < CH; ++j) slot[j * BW] = __uint_as_float(v[j]);
+                    } else {
+                        float acc[CH];
+#pragma unroll
+                        for (int j = 0; j < CH; ++j) acc[j] = __uint_as_float(v[j]);
+                        for (int c = cta + 1; c <= c_last; ++c) {
+                            const float* slot = ws_part + (int64_t)c * BT * BW + (int64_t)c0 * BW + row_in_tile;
+                            float p[CH];
+#pragma unroll
+                            for (int j = 0; j < CH; ++j) p[j] = __ldcg(slot + j * BW);
+#pragma unroll
+                            for (int j = 0; j < CH; ++j) acc[j] += p[j];
+                        }
+                        if (wrow < w.rows) {
+                            float* o = out + (m0 + c0) * ldo + wrow;
+                            const int64_t mleft = m - (m0 + c0);
+#pragma unroll
+                            for (int j = 0; j < CH; ++j)
+                                if (j < mleft) o[j * ldo] = acc[j];
                         }
                     }
                 }
+                if (contributor) {
+                    __threadfence();
+                    epi_bar();
+                    if (threadIdx.x == 32 * EPI_WARP0) st_release(ws_flag + cta, 1u);
+                } else if (owner) {
+                    epi_bar();  // all partial reads done: clear the flags for the next launch
+                    if (threadIdx.x == 32 * EPI_WARP0)
+                        for (int c = cta + 1; c <= c_last; ++c) ws_flag[c] = 0u;
+                }
             }
+            tc_fence_before();
+            __syncwarp();
+            JK_TRACE_POINT(8, seg_i);
+            if (lane == 0) mbar_arrive(acc_empty(b));
+            ++seg_i;
+        }
+    } else {
+        // ------------------------------ dequantizers ------------------------------
+        if constexpr (QUANT) {
+            const int t = threadIdx.x - 32 * DQ_WARP0;  // 0..255
+            const int row_in_tile = t & (BW - 1);
+            if (t < BW) dequant_role<FMT, BF16, BT, 0>(sched, ss, smem, row_in_tile, w, err, ok, bar0, lane);
+            else dequant_role<FMT, BF16, BT, 1>(sched, ss, smem, row_in_tile, w, err, ok, bar0, lane);
         }
     }
 
     tc_fence_before();
     __syncthreads();
-    if (warp == 1) {
+    if (warp == MMA_WARP) {
         tc_fence_after();
         tmem_dealloc(tmem, TMEM_COLS);
     }
 }
 
+// Shared-memory opt-in and CTAs per SM, once per (kernel instantiation, device): `cache` must be
+// a static of the instantiation's own launcher (all instantiations share one function type).
+template <class K>
+int prepare_kernel(K kern, int smem, int device, int (&cache)[64]) {
+    if (device < 0 || device >= 64) return -1;
+    if (cache[device] == 0) {
+        if (cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, smem) != cudaSuccess) return -1;
+        int per_sm = 0;
+        if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, kern, THREADS, smem) != cudaSuccess || per_sm < 1)
+            return -1;
+        cache[device] = per_sm;
+    }
+    return cache[device];
+}
+
+struct LaunchArgs {
+    const jk_qmatrix* wq;
+    const CUtensorMap* tm_x;
+    float* out;
+    int64_t m, ldo;
+    bool stream_k;
+    float* ws_part;
+    uint32_t* ws_flag;
+    int grid_cap;  // 0 = SM count x occupancy
+    cudaStream_t stream;
+};
+
 template <int FMT, bool BF16, int BT>
-jk_status launch_tc(const jk_qmatrix* wq, const CUtensorMap& tm_x, float* out, int64_t m, int64_t ldo,
-                    int64_t part_stride, int splits, cudaStream_t stream) {
+jk_status launch_tc(const LaunchArgs& a) {
     using L = Smem<FMT, BT>;
     auto kern = gemm_tc_kernel<FMT, BF16, BT>;
-    static int attr_device_mask = 0;  // devices on which the smem attribute is set (set once each)
     int dev = 0;
     cudaGetDevice(&dev);
-    if (dev >= 31 || !(attr_device_mask & (1 << dev))) {
-        cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, L::total);
-        if (e != cudaSuccess) return cuda_fail(e, "gemm smem attribute");
-        if (dev < 31) attr_device_mask |= 1 << dev;
-    }
-    const WView& w = wq->view;
-    const int kb_total = (int)(w.k / KB);
-    dim3 grid((unsigned)((w.rows + BW - 1) / BW), (unsigned)((m + BT - 1) / BT), (unsigned)splits);
-    kern<<<grid, THREADS, L::total, stream>>>(tm_x, wq->tm_w, w, out, m, ldo, part_stride, kb_total, splits,
-                                              device_error_word(wq->device));
+    static int per_sm_cache[64] = {};
+    const int per_sm = prepare_kernel(kern, L::total, dev, per_sm_cache);
+    if (per_sm < 0) return cuda_fail(cudaGetLastError(), "gemm kernel attributes");
+    const WView& w = a.wq->view;
+    Sched s;
+    s.tiles_m = (int)((a.m + BT - 1) / BT);
+    s.tiles = ((w.rows + BW - 1) / BW) * s.tiles_m;
+    s.kbt = (int)(w.k / KB);
+    s.sk = a.stream_k ? 1 : 0;
+    int64_t g = (int64_t)sm_count(dev) * per_sm;
+    if (a.grid_cap > 0 && g > a.grid_cap) g = a.grid_cap;
+    const int64_t work = s.sk ? s.tiles * s.kbt : s.tiles;
+    if (g > work) g = work;
+    s.G = (int)g;
+    kern<<<s.G, THREADS, L::total, a.stream>>>(*a.tm_x, a.wq->tm_w, w, a.out, a.m, a.ldo, s, a.ws_part, a.ws_flag,
+                                               device_error_word(a.wq->device));
     return cuda_fail(cudaGetLastError(), "gemm launch");
 }
 
 template <int FMT, bool BF16>
-jk_status launch_tc_bt(const jk_qmatrix* wq, const CUtensorMap& tm_x, float* out, int64_t m, int64_t ldo,
-                       int64_t part_stride, int splits, int bt, cudaStream_t stream) {
+jk_status launch_tc_bt(const LaunchArgs& a, int bt) {
     switch (bt) {
-    case 32: return launch_tc<FMT, BF16, 32>(wq, tm_x, out, m, ldo, part_stride, splits, stream);
-    case 64: return launch_tc<FMT, BF16, 64>(wq, tm_x, out, m, ldo, part_stride, splits, stream);
-    case 128: return launch_tc<FMT, BF16, 128>(wq, tm_x, out, m, ldo, part_stride, splits, stream);
-    default: return launch_tc<FMT, BF16, 256>(wq, tm_x, out, m, ldo, part_stride, splits, stream);
+    case 32: return launch_tc<FMT, BF16, 32>(a);
+    case 64: return launch_tc<FMT, BF16, 64>(a);
+    case 128: return launch_tc<FMT, BF16, 128>(a);
+    default: return launch_tc<FMT, BF16, 256>(a);
     }
 }
 
 template <bool BF16>
-jk_status launch_tc_fmt(const jk_qmatrix* wq, const CUtensorMap& tm_x, float* out, int64_t m, int64_t ldo,
-                        int64_t part_stride, int splits, int bt, cudaStream_t stream) {
-    switch (wq->view.fmt) {
-    case FMT_Q4K: return launch_tc_bt<FMT_Q4K, BF16>(wq, tm_x, out, m, ldo, part_stride, splits, bt, stream);
-    case FMT_Q6K: return launch_tc_bt<FMT_Q6K, BF16>(wq, tm_x, out, m, ldo, part_stride, splits, bt, stream);
-    case FMT_Q8_0: return launch_tc_bt<FMT_Q8_0, BF16>(wq, tm_x, out, m, ldo, part_stride, splits, bt, stream);
-    case FMT_Q5_0: return launch_tc_bt<FMT_Q5_0, BF16>(wq, tm_x, out, m, ldo, part_stride, splits, bt, stream);
-    default: return launch_tc_bt<FMT_F16, BF16>(wq, tm_x, out, m, ldo, part_stride, splits, bt, stream);
+jk_status launch_tc_fmt(const LaunchArgs& a, int bt) {
+    switch (a.wq->view.fmt) {
+    case FMT_Q4K: return launch_tc_bt<FMT_Q4K, BF16>(a, bt);
+    case FMT_Q6K: return launch_tc_bt<FMT_Q6K, BF16>(a, bt);
+    case FMT_Q8_0: return launch_tc_bt<FMT_Q8_0, BF16>(a, bt);
+    case FMT_Q5_0: return launch_tc_bt<FMT_Q5_0, BF16>(a, bt);
+    default: return launch_tc_bt<FMT_F16, BF16>(a, bt);
     }
 }
 
@@ -399,8 +754,19 @@ jk_status make_weight_tmap(const WView& w, CUtensorMap* map) {
     }
 }
 
-jk_status launch_gemm(const jk_qmatrix* w, const void* x, bool x_bf16, size_t m, float* out, int bt, int splits,
-                      float* part, cudaStream_t stream) {
+// Stream-K workspace layout: first one u32 flag per CTA (at most 2 CTAs per SM), padded to 256
+// bytes -- at a fixed offset so the flags are the same words whatever the tile shape, and zero
+// between launches (the kernel leaves them zero) -- then one BT x 128 f32 partial tile per CTA.
+size_t stream_k_flag_bytes(int device) {
+    return ((size_t)sm_count(device) * 2 * 4 + 255) / 256 * 256;
+}
+
+size_t stream_k_workspace_bytes(int device, int bt) {
+    return stream_k_flag_bytes(device) + (size_t)sm_count(device) * 2 * (size_t)bt * BW * 4;
+}
+
+jk_status launch_gemm(const jk_qmatrix* w, const void* x, bool x_bf16, size_t m, float* out, int bt, bool stream_k,
+                      void* workspace, size_t workspace_bytes, cudaStream_t stream) {
     if (m == 0) return JK_OK;
     if (!w->has_tmap) return fail(JK_ERR_INVALID, "matrix has no tensor-core layout");
     CUtensorMap tm_x;
@@ -408,17 +774,24 @@ jk_status launch_gemm(const jk_qmatrix* w, const void* x, bool x_bf16, size_t m,
                                   (uint64_t)w->k, (uint64_t)m, (uint64_t)w->k * 2, KB, (uint32_t)bt,
                                   CU_TENSOR_MAP_SWIZZLE_128B, x);
     if (st != JK_OK) return st;
-    const int64_t ldo = w->view.rows;
-    const int64_t len = (int64_t)m * ldo;
-    float* target = splits > 1 ? part : out;
-    st = x_bf16 ? launch_tc_fmt<true>(w, tm_x, target, (int64_t)m, ldo, len, splits, bt, stream)
-                : launch_tc_fmt<false>(w, tm_x, target, (int64_t)m, ldo, len, splits, bt, stream);
-    if (st != JK_OK) return st;
-    if (splits > 1) {
-        reduce_splits_kernel<<<(unsigned)((len + 255) / 256), 256, 0, stream>>>(part, out, len, splits);
-        return cuda_fail(cudaGetLastError(), "reduce_splits launch");
+    LaunchArgs a{};
+    a.wq = w;
+    a.tm_x = &tm_x;
+    a.out = out;
+    a.m = (int64_t)m;
+    a.ldo = w->view.rows;
+    a.stream = stream;
+    a.stream_k = stream_k;
+    if (stream_k) {
+        int dev = 0;
+        cudaGetDevice(&dev);
+        if (!workspace || workspace_bytes < stream_k_workspace_bytes(dev, bt))
+            return fail(JK_ERR_INVALID, "stream-K workspace too small");
+        a.ws_flag = static_cast<uint32_t*>(workspace);
+        a.ws_part = reinterpret_cast<float*>(static_cast<char*>(workspace) + stream_k_flag_bytes(dev));
+        a.grid_cap = sm_count(dev) * 2;
     }
-    return JK_OK;
+    return x_bf16 ? launch_tc_fmt<true>(a, bt) : launch_tc_fmt<false>(a, bt);
 }
 
 }  // namespace jk

@@ -53,10 +53,14 @@ jk_status launch_gemv(const WView& w, const void* x, int x_dtype, size_t m, floa
                       cudaStream_t stream);
 // Weight tensor map for the tensor-core kernel (stored in the qmatrix at creation).
 jk_status make_weight_tmap(const WView& w, CUtensorMap* map);
-// Tensor-core GEMM: bt = activation-row tile (32/64/128/256); x is bf16 or f16 [m][k];
-// splits > 1 writes partials to `part` ([splits][m][n] f32) and reduces them into `out`.
-jk_status launch_gemm(const jk_qmatrix* w, const void* x, bool x_bf16, size_t m, float* out,
-                      int bt, int splits, float* part, cudaStream_t stream);
+// Tensor-core GEMM: bt = activation-row tile (32/64/128/256); x is bf16 or f16 [m][k].
+// stream_k selects the stream-K schedule (K split across CTAs, partials combined in-kernel in
+// fixed k order), which needs `workspace` of stream_k_workspace_bytes() whose first
+// stream_k_flag_bytes() are zero; otherwise whole tiles per CTA (row invariant).
+size_t stream_k_flag_bytes(int device);
+size_t stream_k_workspace_bytes(int device, int bt);
+jk_status launch_gemm(const jk_qmatrix* w, const void* x, bool x_bf16, size_t m, float* out, int bt,
+                      bool stream_k, void* workspace, size_t workspace_bytes, cudaStream_t stream);
 jk_status launch_convert_to_bf16(const void* x, int x_dtype, size_t count, void* out,
                                  cudaStream_t stream);
 

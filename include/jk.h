@@ -190,6 +190,28 @@ jk_status jk_matmul_tiled(const jk_qmatrix *w, const void *x, int x_dtype, size_
 jk_status jk_f16_linear(const void *x_f16, size_t m, size_t k, const void *w_f16, size_t n,
                         float *out, void *stream);
 
+/* ---- allocation-free product ----------------------------------------------------------------- */
+
+/* Size of the device buffer libjk.so declares for jk_matmul_splitk_noalloc (per GPU, held from
+ * library load until process exit). */
+#define JK_NOALLOC_SCRATCH_BYTES (20u * 1024u * 1024u)
+
+/* No counterpart in the reference: an addition for callers that cannot allocate device memory
+ * while they run a product -- code under a framework that owns every device allocation (a
+ * cudaMalloc from the library would escape its accounting or exceed its cap), code inside a
+ * stream capture, or paths where the device synchronisation of a cudaMalloc is not acceptable.
+ * Computes the same product as jk_matmul_plan with plan {bm, 128, splits > 1} (the stream-K
+ * schedule), with its scratch in a fixed buffer inside the library instead of a jk_split_scratch;
+ * it calls no cudaMalloc, cudaFree or allocating routine. Activations must be bf16 or f16
+ * (JK_ERR_UNSUPPORTED for f32). Limit: the schedule runs one CTA per SM and needs a bm x 128 f32
+ * partial tile per CTA, bm * 512 bytes each; if that exceeds JK_NOALLOC_SCRATCH_BYTES minus 4096
+ * bytes of flag words (never on a 148-SM B200) the call fails with JK_ERR_SHAPE and launches
+ * nothing. The first call on a device looks up the buffer's device address (cudaGetSymbolAddress,
+ * no allocation); make that first call outside any stream capture. All calls on a device share
+ * the buffer: calls that can overlap on the GPU race -- order them on one stream. */
+jk_status jk_matmul_splitk_noalloc(const jk_qmatrix *w, const void *x, int x_dtype, size_t x_len, size_t m,
+                                   float *out, size_t out_len, int bm, void *stream);
+
 #ifdef __cplusplus
 }
 #endif

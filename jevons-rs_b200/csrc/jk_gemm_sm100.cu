@@ -37,6 +37,8 @@
 
 #include <cudaTypedefs.h>
 
+#include <cstdio>
+
 namespace jk {
 
 namespace {
@@ -791,6 +793,48 @@ jk_status launch_gemm(const jk_qmatrix* w, const void* x, bool x_bf16, size_t m,
         a.ws_part = reinterpret_cast<float*>(static_cast<char*>(workspace) + stream_k_flag_bytes(dev));
         a.grid_cap = sm_count(dev) * 2;
     }
+    return x_bf16 ? launch_tc_fmt<true>(a, bt) : launch_tc_fmt<false>(a, bt);
+}
+
+// Stream-K launch on a workspace of fixed capacity provided by the caller: flag words at `flags`
+// (zero on entry), partial tiles at `partials`, room for `max_ctas` partial tiles. Fails with
+// JK_ERR_SHAPE, launching nothing, if the grid this device runs needs more partial tiles.
+jk_status launch_gemm_stream_k_fixed(const jk_qmatrix* w, const void* x, bool x_bf16, size_t m, float* out, int bt,
+                                     uint32_t* flags, float* partials, int max_ctas, size_t capacity_bytes,
+                                     cudaStream_t stream) {
+    if (m == 0) return JK_OK;
+    if (!w->has_tmap) return fail(JK_ERR_INVALID, "matrix has no tensor-core layout");
+    int dev = 0;
+    cudaGetDevice(&dev);
+    // the grid the stream-K schedule uses: one CTA per SM (every instantiation runs one per SM),
+    // never more CTAs than (tile, k-block) iterations
+    const int64_t tiles = ((w->view.rows + BW - 1) / BW) * (((int64_t)m + bt - 1) / bt);
+    int64_t g = sm_count(dev);
+    if (g > tiles * (w->k / KB)) g = tiles * (w->k / KB);
+    if (g > max_ctas) {
+        char buf[200];
+        snprintf(buf, sizeof buf,
+                 "stream-K product with bm=%d on this device needs %lld partial tiles (%lld bytes of scratch); "
+                 "the allocation-free buffer holds %zu bytes",
+                 bt, (long long)g, (long long)(g * bt * BW * 4), capacity_bytes);
+        return fail(JK_ERR_SHAPE, buf);
+    }
+    CUtensorMap tm_x;
+    jk_status st = encode_tmap_2d(&tm_x, x_bf16 ? CU_TENSOR_MAP_DATA_TYPE_BFLOAT16 : CU_TENSOR_MAP_DATA_TYPE_FLOAT16,
+                                  (uint64_t)w->k, (uint64_t)m, (uint64_t)w->k * 2, KB, (uint32_t)bt,
+                                  CU_TENSOR_MAP_SWIZZLE_128B, x);
+    if (st != JK_OK) return st;
+    LaunchArgs a{};
+    a.wq = w;
+    a.tm_x = &tm_x;
+    a.out = out;
+    a.m = (int64_t)m;
+    a.ldo = w->view.rows;
+    a.stream = stream;
+    a.stream_k = true;
+    a.ws_flag = flags;
+    a.ws_part = partials;
+    a.grid_cap = (int)g;
     return x_bf16 ? launch_tc_fmt<true>(a, bt) : launch_tc_fmt<false>(a, bt);
 }
 

@@ -61,6 +61,9 @@ size_t stream_k_flag_bytes(int device);
 size_t stream_k_workspace_bytes(int device, int bt);
 jk_status launch_gemm(const jk_qmatrix* w, const void* x, bool x_bf16, size_t m, float* out, int bt,
                       bool stream_k, void* workspace, size_t workspace_bytes, cudaStream_t stream);
+jk_status launch_gemm_stream_k_fixed(const jk_qmatrix* w, const void* x, bool x_bf16, size_t m, float* out, int bt,
+                                     uint32_t* flags, float* partials, int max_ctas, size_t capacity_bytes,
+                                     cudaStream_t stream);
 jk_status launch_convert_to_bf16(const void* x, int x_dtype, size_t count, void* out,
                                  cudaStream_t stream);
 

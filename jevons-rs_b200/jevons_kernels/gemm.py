@@ -258,6 +258,14 @@ def matvec(gpu: Gpu, x: Buf, m: int, w: QMatrix, out: Buf, dummy=None) -> None:
     check(load().jk_matvec(w.handle, xp, xt, xl, m, op, ol, _stream()))
 
 
+def matmul_splitk_noalloc(gpu: Gpu, x: Buf, m: int, w: QMatrix, out: Buf, bm: int = 256) -> None:
+    """Split-K (stream-K) product whose scratch is a fixed buffer inside the library, for callers
+    that cannot allocate device memory while the product runs (no cudaMalloc / cudaFree is made).
+    bf16 or f16 activations; calls on one device must not overlap on the GPU (they share the buffer)."""
+    xp, xt, xl, op, ol = _args(x, out)
+    check(load().jk_matmul_splitk_noalloc(w.handle, xp, xt, xl, m, op, ol, int(bm), _stream()))
+
+
 def f16_linear(x: torch.Tensor, weight: torch.Tensor) -> torch.Tensor:
     """jevons_burn::kernels::f16_linear (kernels.rs:107-114): f32 x @ weight^T with FP16 weight [N, K].
 
@@ -287,4 +295,4 @@ def f16_linear_scaled(x: torch.Tensor, weight: torch.Tensor) -> torch.Tensor:
 
 
 __all__ = ["GEMV_ROWS", "Gpu", "Buf", "QMatrix", "Plan", "SplitScratch", "matmul", "matmul_plan", "matmul_tiled",
-           "matvec", "f16_linear", "f16_linear_scaled", "tile_n", "TensorType", "block", "pack", "JkError"]
+           "matvec", "matmul_splitk_noalloc", "f16_linear", "f16_linear_scaled", "tile_n", "TensorType", "block", "pack", "JkError"]

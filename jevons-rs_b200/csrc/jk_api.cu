@@ -398,9 +398,11 @@ jk_status upload_layout(int device, int type, size_t n, size_t k, size_t experts
     m->experts = experts;
     m->view.fmt = fmt_of(type);
     const size_t d_bytes = hl.d.size() * 2, h_bytes = hl.h.size() * 4;
+    // The small-row kernel copies the scale / high-bit words of a row segment rounded out to
+    // 16-byte boundaries, so those arrays carry 64 bytes of slack past their end.
     cudaError_t e = cudaMalloc(&m->q_alloc, q_bytes ? q_bytes : 16);
-    if (e == cudaSuccess && d_bytes) e = cudaMalloc(&m->d_alloc, d_bytes);
-    if (e == cudaSuccess && h_bytes) e = cudaMalloc(&m->h_alloc, h_bytes);
+    if (e == cudaSuccess && d_bytes) e = cudaMalloc(&m->d_alloc, d_bytes + 64);
+    if (e == cudaSuccess && h_bytes) e = cudaMalloc(&m->h_alloc, h_bytes + 64);
     if (e == cudaSuccess) e = cudaMemcpy(m->q_alloc, q_src, q_bytes, cudaMemcpyHostToDevice);
     if (e == cudaSuccess && d_bytes) e = cudaMemcpy(m->d_alloc, hl.d.data(), d_bytes, cudaMemcpyHostToDevice);
     if (e == cudaSuccess && h_bytes) e = cudaMemcpy(m->h_alloc, hl.h.data(), h_bytes, cudaMemcpyHostToDevice);

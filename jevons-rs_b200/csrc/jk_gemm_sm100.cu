@@ -429,6 +429,7 @@ gemm_tc_kernel(const __grid_constant__ CUtensorMap tm_x, const __grid_constant__
     __syncthreads();
     tc_fence_after();
     const uint32_t tmem = *tmem_holder;
+    JK_TRACE_POINT(14, 0);
 
     bool ok = true;
     SegState ss;
@@ -538,6 +539,7 @@ gemm_tc_kernel(const __grid_constant__ CUtensorMap tm_x, const __grid_constant__
             if (!ok) break;
             if (leader) mma_commit(acc_full(b));  // arrives when this segment's MMAs are complete
             __syncwarp();
+            JK_TRACE_POINT(12, seg_i);
             ++seg_i;
         }
         if (!ok && issued) {
@@ -586,6 +588,7 @@ gemm_tc_kernel(const __grid_constant__ CUtensorMap tm_x, const __grid_constant__
                 }
                 epi_bar();
                 ok = flags_ok != 0;
+                JK_TRACE_POINT(10, seg_i);
             }
             if (ok) {
                 const uint32_t tbase = tmem + ((uint32_t)(32 * quarter) << 16) + (uint32_t)(b * BT);
@@ -626,6 +629,7 @@ gemm_tc_kernel(const __grid_constant__ CUtensorMap tm_x, const __grid_constant__
                         }
                     }
                 }
+                JK_TRACE_POINT(11, seg_i);
                 if (contributor) {
                     __threadfence();
                     epi_bar();
@@ -654,6 +658,7 @@ gemm_tc_kernel(const __grid_constant__ CUtensorMap tm_x, const __grid_constant__
 
     tc_fence_before();
     __syncthreads();
+    JK_TRACE_POINT(15, 0);
     if (warp == MMA_WARP) {
         tc_fence_after();
         tmem_dealloc(tmem, TMEM_COLS);

@@ -74,7 +74,18 @@ struct Smem {
     static constexpr int off_a = off_b + S * B_STAGE;
     static constexpr int off_raw = off_a + S * A_STAGE_BYTES;
     static constexpr int off_bar = off_raw + R * raw_bytes;
-    static constexpr int n_bar = 3 * S + 2 * R + 4;  // full_b, full_a, empty | raw_full/empty | acc_full/empty x2
+    // Stream-K fix-up: an owner's final segment is the CTA's last, so by then the operand and raw
+    // stages [0, off_bar) are idle. They hold a ring of FIX_NB chunks for the contributor partials
+    // (bulk-copied, FIX_CH activation rows x BW f32 each, contiguous in the workspace), then two
+    // output staging buffers of the same size from which whole 512-byte output rows are written
+    // by bulk stores.
+    static constexpr int FIX_CH = BT < 64 ? BT : 64;
+    static constexpr int FIX_CHUNK = FIX_CH * BW * 4;
+    static constexpr int FIX_NB = off_bar / FIX_CHUNK - 2 < 16 ? off_bar / FIX_CHUNK - 2 : 16;
+    static constexpr int off_fix_out = FIX_NB * FIX_CHUNK;
+    static_assert(FIX_NB >= 1, "fix-up ring");
+    // full_b, full_a, empty | raw_full/empty | acc_full/empty x2 | fix-up chunk ring
+    static constexpr int n_bar = 3 * S + 2 * R + 4 + FIX_NB;
     static constexpr int off_tmem = off_bar + 8 * n_bar;
     static constexpr int total = off_tmem + 16 + 1024;  // + base alignment slack
     static_assert(total <= SMEM_LIMIT, "shared memory budget");
@@ -114,6 +125,20 @@ __device__ __forceinline__ void seg_init(const Sched& s, int c, SegState& st) {
         st.end = s.tiles;
     }
 }
+
+__device__ __forceinline__ void bulk_g2s(uint32_t dst, const void* src, uint32_t bytes, uint32_t bar) {
+    asm volatile("cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];"
+                 :: "r"(dst), "l"(src), "r"(bytes), "r"(bar) : "memory");
+}
+
+__device__ __forceinline__ void bulk_s2g(void* dst, uint32_t src, uint32_t bytes) {
+    asm volatile("cp.async.bulk.global.shared::cta.bulk_group [%0], [%1], %2;" :: "l"(dst), "r"(src), "r"(bytes) : "memory");
+}
+__device__ __forceinline__ void bulk_commit() { asm volatile("cp.async.bulk.commit_group;" ::: "memory"); }
+// wait until at most N committed bulk groups of this thread still read their shared-memory source
+template <int N>
+__device__ __forceinline__ void bulk_wait_read() { asm volatile("cp.async.bulk.wait_group.read %0;" :: "n"(N) : "memory"); }
+__device__ __forceinline__ void bulk_wait_all() { asm volatile("cp.async.bulk.wait_group 0;" ::: "memory"); }
 
 __device__ __forceinline__ bool seg_next(const Sched& s, SegState& st, Seg& g) {
     if (st.next >= st.end) return false;
@@ -399,6 +424,7 @@ gemm_tc_kernel(const __grid_constant__ CUtensorMap tm_x, const __grid_constant__
     auto raw_empty = [&](int r) { return bar0 + 8u * (3 * S + R + r); };
     auto acc_full = [&](int b) { return bar0 + 8u * (3 * S + 2 * R + b); };
     auto acc_empty = [&](int b) { return bar0 + 8u * (3 * S + 2 * R + 2 + b); };
+    auto fix_full = [&](int i) { return bar0 + 8u * (3 * S + 2 * R + 4 + i); };
     uint32_t* tmem_holder = reinterpret_cast<uint32_t*>(smem + L::off_tmem);
 
     const int warp = threadIdx.x >> 5;
@@ -419,6 +445,7 @@ gemm_tc_kernel(const __grid_constant__ CUtensorMap tm_x, const __grid_constant__
             mbar_init(acc_full(b), 1);
             mbar_init(acc_empty(b), EPI_WARPS);
         }
+        for (int i = 0; i < L::FIX_NB; ++i) mbar_init(fix_full(i), 1);
         mbar_fence_init();
     }
     if (warp == MMA_WARP) {
@@ -554,7 +581,12 @@ gemm_tc_kernel(const __grid_constant__ CUtensorMap tm_x, const __grid_constant__
         // ------------------------------ epilogue ------------------------------
         const int quarter = warp & 3;                 // TMEM lanes this warp may read
         const int row_in_tile = 32 * quarter + lane;  // weight row within the tile
+        const bool issuer = threadIdx.x == 32 * EPI_WARP0;
+        // output rows are 16-byte aligned: the owner fix-up writes them with bulk stores
+        const bool vec_out = ((reinterpret_cast<uintptr_t>(out) | (uintptr_t)(ldo * 4)) & 15) == 0;
+        __shared__ int fix_bad;
         int seg_i = 0;
+        int fix_q = 0;  // fix-up chunks consumed so far (ring parity)
         while (ok && seg_next(sched, ss, sg)) {
             const int b = seg_i & 1;
             ok = __all_sync(0xFFFFFFFFu, mbar_wait_sleepy(acc_full(b), (seg_i >> 1) & 1, err));
@@ -594,7 +626,29 @@ gemm_tc_kernel(const __grid_constant__ CUtensorMap tm_x, const __grid_constant__
                 const uint32_t tbase = tmem + ((uint32_t)(32 * quarter) << 16) + (uint32_t)(b * BT);
                 // CH columns per round: all TMEM loads of the round are issued before one wait, and an
                 // owner loads all contributor partials of the round before adding them.
-                constexpr int CH = BT < 64 ? BT : 64;
+                constexpr int CH = L::FIX_CH;
+                // Owner of the CTA's last segment: the contributor partials arrive in shared memory by
+                // bulk copies (round-major, contributor-minor chunks through a FIX_NB ring) instead of
+                // per-thread loads, so a whole ring of them is in flight at once.
+                const int nc = c_last - cta;
+                const bool bulk_fix = owner && nc > 0 && ss.next >= ss.end;
+                const int nchunks = bulk_fix ? (BT / CH) * nc : 0;
+                auto issue_chunk = [&](int q) {
+                    const int r = q / nc, ci = q - r * nc;
+                    const int g = fix_q + q, buf = g % L::FIX_NB;
+                    const float* src = ws_part + (int64_t)(cta + 1 + ci) * BT * BW + (int64_t)(r * CH) * BW;
+                    mbar_expect_tx(fix_full(buf), (uint32_t)L::FIX_CHUNK);
+                    bulk_g2s(sbase + (uint32_t)(buf * L::FIX_CHUNK), src, (uint32_t)L::FIX_CHUNK, fix_full(buf));
+                };
+                int issued_q = 0;
+                bool dead = false;
+                if (bulk_fix) {
+                    if (issuer) {
+                        fix_bad = 0;
+                        fence_proxy_async_smem();
+                        for (; issued_q < nchunks && issued_q < L::FIX_NB; ++issued_q) issue_chunk(issued_q);
+                    }
+                }
 #pragma unroll 1
                 for (int c0 = 0; c0 < BT; c0 += CH) {
                     uint32_t v[CH];
@@ -604,6 +658,7 @@ gemm_tc_kernel(const __grid_constant__ CUtensorMap tm_x, const __grid_constant__
                         tmem_ld16(tbase + (uint32_t)(c0 + 16 * q), vq);
                     }
                     tmem_ld_wait();
+                    JK_TRACE_POINT(5, c0 / CH);
                     if (contributor) {
                         float* slot = ws_part + (int64_t)cta * BT * BW + (int64_t)c0 * BW + row_in_tile;
 #pragma unroll
@@ -612,15 +667,51 @@ gemm_tc_kernel(const __grid_constant__ CUtensorMap tm_x, const __grid_constant__
                         float acc[CH];
 #pragma unroll
                         for (int j = 0; j < CH; ++j) acc[j] = __uint_as_float(v[j]);
-                        for (int c = cta + 1; c <= c_last; ++c) {
-                            const float* slot = ws_part + (int64_t)c * BT * BW + (int64_t)c0 * BW + row_in_tile;
-                            float p[CH];
+                        if (bulk_fix) {
+                            for (int ci = 0; ci < nc; ++ci) {
+                                const int q = (c0 / CH) * nc + ci;
+                                const int g = fix_q + q, buf = g % L::FIX_NB;
+                                if (!dead) dead = !mbar_wait(fix_full(buf), (uint32_t)((g / L::FIX_NB) & 1), err);
+                                if (!dead) {
+                                    const float* sp = reinterpret_cast<const float*>(smem + buf * L::FIX_CHUNK) + row_in_tile;
 #pragma unroll
-                            for (int j = 0; j < CH; ++j) p[j] = __ldcg(slot + j * BW);
+                                    for (int j = 0; j < CH; ++j) acc[j] += sp[j * BW];
+                                }
+                                epi_bar();  // every reader is done with this buffer
+                                if (issuer && !dead && issued_q < nchunks) {
+                                    fence_proxy_async_smem();
+                                    issue_chunk(issued_q++);
+                                }
+                            }
+                        } else {
+                            for (int c = cta + 1; c <= c_last; ++c) {
+                                const float* slot = ws_part + (int64_t)c * BT * BW + (int64_t)c0 * BW + row_in_tile;
+                                float p[CH];
 #pragma unroll
-                            for (int j = 0; j < CH; ++j) acc[j] += p[j];
+                                for (int j = 0; j < CH; ++j) p[j] = __ldcg(slot + j * BW);
+#pragma unroll
+                                for (int j = 0; j < CH; ++j) acc[j] += p[j];
+                            }
                         }
-                        if (wrow < w.rows) {
+                        JK_TRACE_POINT(13, c0 / CH);
+                        if (bulk_fix && vec_out) {
+                            // stage the round as [row of out][BW] and write whole rows with bulk
+                            // stores; the two staging buffers alternate between rounds
+                            float* tp = reinterpret_cast<float*>(smem + L::off_fix_out + ((c0 / CH) & 1) * L::FIX_CHUNK);
+                            if (lane == 0) bulk_wait_read<1>();  // this buffer's stores of two rounds ago
+                            epi_bar();
+#pragma unroll
+                            for (int j = 0; j < CH; ++j) tp[j * BW + row_in_tile] = acc[j];
+                            fence_proxy_async_smem();
+                            epi_bar();
+                            if (lane == 0) {
+                                const int64_t mleft = m - (m0 + c0);
+                                const int64_t cols = w.rows - n0 < BW ? w.rows - n0 : BW;
+                                for (int j = quarter; j < CH && j < mleft; j += EPI_WARPS)
+                                    bulk_s2g(out + (m0 + c0 + j) * ldo + n0, smem_u32(tp + j * BW), (uint32_t)(cols * 4));
+                                bulk_commit();
+                            }
+                        } else if (wrow < w.rows) {
                             float* o = out + (m0 + c0) * ldo + wrow;
                             const int64_t mleft = m - (m0 + c0);
 #pragma unroll
@@ -629,11 +720,30 @@ gemm_tc_kernel(const __grid_constant__ CUtensorMap tm_x, const __grid_constant__
                         }
                     }
                 }
+                if (bulk_fix) {
+                    if (vec_out && lane == 0) bulk_wait_all();  // output rows written before the flags clear
+                    if (dead) atomicOr(&fix_bad, 1);
+                    epi_bar();
+                    if (fix_bad) {
+                        ok = false;
+                        // a chunk never arrived: give the copies still in flight a bounded wait
+                        if (issuer)
+                            for (int q = 0; q < issued_q; ++q) {
+                                const int g = fix_q + q;
+                                (void)mbar_wait(fix_full(g % L::FIX_NB), (uint32_t)((g / L::FIX_NB) & 1), err);
+                            }
+                    }
+                    fix_q += nchunks;
+                }
                 JK_TRACE_POINT(11, seg_i);
                 if (contributor) {
-                    __threadfence();
+                    // every partial store of the tile precedes the barrier; one gpu-scope fence by
+                    // the flag writer then publishes them all (cumulativity through bar.sync)
                     epi_bar();
-                    if (threadIdx.x == 32 * EPI_WARP0) st_release(ws_flag + cta, 1u);
+                    if (issuer) {
+                        __threadfence();
+                        st_release(ws_flag + cta, 1u);
+                    }
                 } else if (owner) {
                     epi_bar();  // all partial reads done: clear the flags for the next launch
                     if (threadIdx.x == 32 * EPI_WARP0)

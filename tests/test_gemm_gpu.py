@@ -214,3 +214,30 @@ def test_config4_vocab_head_sampled_and_linear(gpu):
     out2 = torch.empty_like(out)
     matmul_plan(gpu, Buf((x * 2).contiguous()), m, w, Buf(out2), None, None, Plan(256, 128, 1))
     assert torch.equal(out2, out * 2)
+
+
+@pytest.mark.parametrize("name,n,k", [("Q4_K", 192, 2560), ("Q8_0", 192, 320), ("Q4_K", 128, 10240), ("Q6_K", 64, 2560)])
+@pytest.mark.parametrize("m", [31, 257])
+def test_stream_k_fixup_shapes(gpu, name, n, k, m):
+    """Stream-K fix-up: partial weight tiles (n % 128 != 0), partial row tiles, tiles split over
+    many CTAs (k = 10240 on one weight tile), and output rows that are not 16-byte aligned (the
+    per-element store path). A spare element after the output must stay untouched."""
+    from jevons_kernels.gemm import Buf, Plan, SplitScratch, matmul_plan
+    w, _, dense = make_weights(gpu, KINDS[name], n, k, seed=n + k + m)
+    x, x_exact = activations(m, k, torch.bfloat16, seed=m + 1)
+    want = oracle.matmul_f64(x_exact, dense)
+    scratch = SplitScratch(gpu)
+    for bm in (32, 256):
+        for splits in (2, 4):
+            assert Plan(bm, 128, splits).valid_for(w, m)
+            for shift in (0, 1):
+                big = torch.full((m * n + 2,), float("nan"), device="cuda")
+                out = big[shift:shift + m * n].view(m, n)
+                matmul_plan(gpu, Buf(x), m, w, Buf(out), None, scratch,
+                            Plan(bm, 128, splits))
+                assert_close(f"{name} {n}x{k} m={m} bm={bm} s={splits} shift={shift}", out.cpu().numpy(), x_exact,
+                             dense, want)
+                assert torch.isnan(big[shift + m * n]).item()
+                if shift:
+                    assert torch.isnan(big[0]).item()
+    assert gpu.device_error() == 0

@@ -229,12 +229,16 @@ def run_ours(args):
 
     from jevons_kernels import synth
     from jevons_kernels.gemm import Buf, Gpu, Plan, QMatrix, SplitScratch, matmul, matvec
+    from jevons_kernels.shard import column_shard, gather_shards
 
     gpu = Gpu(local)
     dev = torch.device("cuda", local)
     L = args.layers
+    # this rank's shard of an (N_DIM * world)-column layer: N_DIM weight rows, seeded by shard
+    lo, hi = column_shard(N_DIM * world, world, rank)
+    assert hi - lo == N_DIM
     rng = np.random.default_rng(1 + 1000 * rank)
-    raw = synth.q4k_blocks(rng, N_DIM, K_DIM)  # this rank's 10240-column shard
+    raw = synth.q4k_blocks(rng, N_DIM, K_DIM)
     # L distinct device copies (distinct memory defeats L2 reuse across the stack)
     ws = [QMatrix.upload(gpu, Q4_K, N_DIM, K_DIM, 1, raw) for _ in range(L)]
     x = torch.from_numpy(synth.activations(np.random.default_rng(2), M_ROWS, K_DIM)).to(dev).bfloat16()
@@ -257,7 +261,7 @@ def run_ours(args):
                 ev.record(cur)
                 comm_stream.wait_event(ev)
                 with torch.cuda.stream(comm_stream):
-                    dist.all_gather_into_tensor(gathered[i], outs[i])
+                    gather_shards(outs[i], out=gathered[i])
         if world > 1:
             ev = torch.cuda.Event()
             ev.record(comm_stream)

@@ -46,9 +46,20 @@ namespace {
 constexpr int BW = 128;                  // weight rows per tile (MMA M)
 constexpr int KB = 64;                   // k-block: one 128-byte swizzle atom of 16-bit values
 constexpr int A_STAGE_BYTES = BW * KB * 2;
-constexpr int PRODUCER_WARP = 0, MMA_WARP = 1, RAW_WARP = 2, EPI_WARP0 = 3, EPI_WARPS = 4, DQ_WARP0 = 7, DQ_WARPS = 8;
-constexpr int THREADS = 32 * (DQ_WARP0 + DQ_WARPS);  // 480
-constexpr int EPI_THREADS = 32 * EPI_WARPS;          // 128: 1 per weight row
+// Warp roles. Warp w is scheduled on SM sub-partition w % 4. The MMA issuer (warp 1) shares its
+// sub-partition only with light roles (an epilogue warp, the raw-weight producer, an idle warp):
+// the dequantizers' large unrolled loops would otherwise keep evicting the issuer's short loop
+// from that sub-partition's instruction cache and stall every MMA issue.
+//   w: 0 producer | 1 MMA | 4..7 epilogue (TMEM lane quarters 0..3) | 9 raw producer | 13 idle
+//      dequantizers 2, 3, 8, 10 (group 0) and 11, 12, 14, 15 (group 1)
+constexpr int PRODUCER_WARP = 0, MMA_WARP = 1, RAW_WARP = 9, EPI_WARP0 = 4, EPI_WARPS = 4, DQ_WARPS = 8;
+constexpr int THREADS = 512;
+constexpr int EPI_THREADS = 32 * EPI_WARPS;  // 128: 1 per weight row
+__device__ __forceinline__ int dq_slot(int warp) {  // position among the dequantizer warps, or -1
+    constexpr unsigned long long tbl = 0x76F543F2FFFF10FFull;  // nibble w: slot, F = not a dequantizer
+    const int v = (int)((tbl >> (4 * warp)) & 15u);
+    return v == 15 ? -1 : v;
+}
 
 template <int FMT>
 struct RawTile {
@@ -61,18 +72,38 @@ struct RawTile {
 
 constexpr int SMEM_LIMIT = 227 * 1024;
 
+// Stage counts. Quantized weights use three rings: SX activation tiles (TMA), SA dequantized weight
+// tiles, R raw super-blocks (TMA). The activation ring is decoupled from the weight ring so that
+// several activation tiles are in flight (their L2 latency is the longest in the loop) while the
+// dequantizers fill a few weight tiles just ahead of the MMA. FP16 weights come by TMA with their
+// activation tile, so for them SX == SA (one coupled ring).
+struct Rings {
+    int sx, sa, r;
+};
+constexpr int SMEM_BUDGET = SMEM_LIMIT - 2048;  // barriers, TMEM holder, 1 KB alignment slack
+constexpr Rings pick_rings(int b_stage, int raw_bytes) {
+    constexpr Rings prio[] = {{8, 4, 4}, {6, 4, 4}, {6, 4, 3}, {6, 3, 3}, {5, 4, 3}, {5, 3, 3}, {4, 4, 3},
+                              {4, 3, 3}, {4, 3, 2}, {4, 2, 3}, {4, 2, 2}, {3, 3, 2}, {3, 2, 2}, {2, 2, 2}};
+    if (raw_bytes == 0) {
+        for (int s = 6; s >= 2; --s)
+            if (s * (b_stage + A_STAGE_BYTES) <= SMEM_BUDGET) return Rings{s, s, 1};
+        return Rings{2, 2, 1};
+    }
+    for (const Rings& c : prio)
+        if (c.sx * b_stage + c.sa * A_STAGE_BYTES + c.r * raw_bytes <= SMEM_BUDGET) return c;
+    return Rings{2, 2, 2};
+}
+
 template <int FMT, int BT>
 struct Smem {
-    static constexpr int S = BT >= 256 ? 3 : 4;  // operand stages (activation tile + weight tile)
     static constexpr int B_STAGE = BT * 128;
     static constexpr int raw_bytes = RawTile<FMT>::bytes;
-    static constexpr int fixed = S * (B_STAGE + A_STAGE_BYTES) + 2048;
-    // raw weight stages: as many as fit (2..4), each one 256-wide super-block of 128 rows
-    static constexpr int R = raw_bytes == 0 ? 1
-                           : (fixed + 4 * raw_bytes <= SMEM_LIMIT ? 4 : fixed + 3 * raw_bytes <= SMEM_LIMIT ? 3 : 2);
+    static constexpr Rings rings = pick_rings(B_STAGE, raw_bytes);
+    static constexpr int SX = rings.sx, SA = rings.sa, R = rings.r;
+    static_assert(FMT != FMT_F16 || SX == SA, "FP16 weights share the activation ring");
     static constexpr int off_b = 0;
-    static constexpr int off_a = off_b + S * B_STAGE;
-    static constexpr int off_raw = off_a + S * A_STAGE_BYTES;
+    static constexpr int off_a = off_b + SX * B_STAGE;
+    static constexpr int off_raw = off_a + SA * A_STAGE_BYTES;
     static constexpr int off_bar = off_raw + R * raw_bytes;
     // Stream-K fix-up: an owner's final segment is the CTA's last, so by then the operand and raw
     // stages [0, off_bar) are idle. They hold a ring of FIX_NB chunks for the contributor partials
@@ -84,8 +115,11 @@ struct Smem {
     static constexpr int FIX_NB = off_bar / FIX_CHUNK - 2 < 16 ? off_bar / FIX_CHUNK - 2 : 16;
     static constexpr int off_fix_out = FIX_NB * FIX_CHUNK;
     static_assert(FIX_NB >= 1, "fix-up ring");
-    // full_b, full_a, empty | raw_full/empty | acc_full/empty x2 | fix-up chunk ring
-    static constexpr int n_bar = 3 * S + 2 * R + 4 + FIX_NB;
+    // full_b/empty_b x SX | full_a/empty_a x SA | raw_full/empty x R | acc_full/empty x 2 | fix-up ring
+    static constexpr int n_bar = 2 * SX + 2 * SA + 2 * R + 4 + FIX_NB;
+    static constexpr int bar_full_b = 0, bar_empty_b = SX, bar_full_a = 2 * SX, bar_empty_a = 2 * SX + SA,
+                         bar_raw_full = 2 * SX + 2 * SA, bar_raw_empty = bar_raw_full + R,
+                         bar_acc_full = bar_raw_empty + R, bar_acc_empty = bar_acc_full + 2, bar_fix = bar_acc_empty + 2;
     static constexpr int off_tmem = off_bar + 8 * n_bar;
     static constexpr int total = off_tmem + 16 + 1024;  // + base alignment slack
     static_assert(total <= SMEM_LIMIT, "shared memory budget");
@@ -179,9 +213,9 @@ __device__ __forceinline__ void tmem_ld16(uint32_t taddr, uint32_t (&v)[16]) {
         : "r"(taddr));
 }
 
-// Per-thread dequantizer of one weight row's super-blocks (256 k-elements = 4 k-blocks). The thread
-// owns half of every k-block (PART 0/1) and writes it, rounded to bf16/f16, into the row's 128-byte
-// swizzled line of the operand tile. Everything a super-block needs beyond the raw TMA stage (block
+// Per-thread dequantizer of one weight row's super-blocks (256 k-elements = 4 k-blocks). A k-block
+// is written in two halves (PART 0/1), rounded to bf16/f16, into the row's 128-byte swizzled line
+// of the operand tile. Everything a super-block needs beyond the raw TMA stage (block
 // scales kept in global memory) is loaded one super-block ahead (prefetch) so no global load sits
 // on the critical path; Q4_K's header is decoded once per super-block into 8 (d*sc, dmin*m) pairs.
 //   Q4_K part p: qs bytes 32j + 16p .. +16 -> low-nibble chunks 2p, 2p+1 and high-nibble chunks
@@ -211,11 +245,11 @@ __device__ __forceinline__ void q4k_vals(uint32_t w0, uint32_t w1, float dd, flo
         }
 }
 
-template <int FMT, bool BF16, int PART>
+template <int FMT, bool BF16>
 struct SbDequant;
 
-template <bool BF16, int PART>
-struct SbDequant<FMT_Q4K, BF16, PART> {
+template <bool BF16>
+struct SbDequant<FMT_Q4K, BF16> {
     float dd[8], mm[8];
     __device__ __forceinline__ void prefetch(const WView&, int64_t, int) {}
     __device__ __forceinline__ void begin(const uint8_t* raw_row, const WView&, int64_t, bool, int) {
@@ -230,7 +264,7 @@ struct SbDequant<FMT_Q4K, BF16, PART> {
             mm[j] = __fmul_rn(dmin, (float)mn);
         }
     }
-    template <int J>
+    template <int J, int PART>
     __device__ __forceinline__ void kblock(const uint8_t* raw_row, int, uint8_t* arow, int sw) {
         const uint4 q = *reinterpret_cast<const uint4*>(raw_row + 16 + 32 * J + 16 * PART);
         float v[8];
@@ -245,8 +279,8 @@ struct SbDequant<FMT_Q4K, BF16, PART> {
     }
 };
 
-template <bool BF16, int PART>
-struct SbDequant<FMT_Q6K, BF16, PART> {
+template <bool BF16>
+struct SbDequant<FMT_Q6K, BF16> {
     uint32_t d_next = 0;
     float d = 0.f;
     __device__ __forceinline__ void prefetch(const WView& w, int64_t rr, int sb) {
@@ -255,7 +289,7 @@ struct SbDequant<FMT_Q6K, BF16, PART> {
     __device__ __forceinline__ void begin(const uint8_t*, const WView&, int64_t, bool row_ok, int) {
         d = row_ok ? half_bits_to_float(d_next) : 0.f;
     }
-    template <int J>
+    template <int J, int PART>
     __device__ __forceinline__ void kblock(const uint8_t* body, int, uint8_t* arow, int sw) {
         Q6KBlock bq;
         bq.load(body, d, J);
@@ -268,8 +302,8 @@ struct SbDequant<FMT_Q6K, BF16, PART> {
     }
 };
 
-template <bool BF16, int PART>
-struct SbDequant<FMT_Q8_0, BF16, PART> {
+template <bool BF16>
+struct SbDequant<FMT_Q8_0, BF16> {
     uint4 d_next = make_uint4(0, 0, 0, 0);  // f16 scales of the super-block's 8 blocks
     uint4 dcur = make_uint4(0, 0, 0, 0);
     __device__ __forceinline__ void prefetch(const WView& w, int64_t rr, int sb) {
@@ -287,7 +321,7 @@ struct SbDequant<FMT_Q8_0, BF16, PART> {
     __device__ __forceinline__ void begin(const uint8_t*, const WView&, int64_t, bool row_ok, int) {
         dcur = row_ok ? d_next : make_uint4(0, 0, 0, 0);
     }
-    template <int J>
+    template <int J, int PART>
     __device__ __forceinline__ void kblock(const uint8_t* raw_row_half0, int row, uint8_t* arow, int sw) {
         // k-block J: 128-byte swizzled half J/2 of the stage (the caller points raw_row_half0 at
         // half 0's row; half 1 starts BW * 128 bytes later), logical chunks 4 (J%2) ..
@@ -304,8 +338,8 @@ struct SbDequant<FMT_Q8_0, BF16, PART> {
     }
 };
 
-template <bool BF16, int PART>
-struct SbDequant<FMT_Q5_0, BF16, PART> {
+template <bool BF16>
+struct SbDequant<FMT_Q5_0, BF16> {
     uint4 d_next = make_uint4(0, 0, 0, 0), h_next0 = make_uint4(0, 0, 0, 0), h_next1 = make_uint4(0, 0, 0, 0);
     uint4 dcur = make_uint4(0, 0, 0, 0), h0 = make_uint4(0, 0, 0, 0), h1 = make_uint4(0, 0, 0, 0);
     __device__ __forceinline__ void prefetch(const WView& w, int64_t rr, int sb) {
@@ -326,7 +360,7 @@ struct SbDequant<FMT_Q5_0, BF16, PART> {
         h0 = h_next0;
         h1 = h_next1;
     }
-    template <int J>
+    template <int J, int PART>
     __device__ __forceinline__ void kblock(const uint8_t* rowp, int, uint8_t* arow, int sw) {
         // 128-byte swizzled row of the super-block; k-block J = logical chunks 2J, 2J+1
         const uint32_t dw = (J >> 1) == 0 ? ((J & 1) ? dcur.y : dcur.x) : ((J & 1) ? dcur.w : dcur.z);
@@ -345,17 +379,21 @@ struct SbDequant<FMT_Q5_0, BF16, PART> {
     }
 };
 
-template <int FMT, bool BF16, int BT, int PART>
-__device__ __forceinline__ void dequant_role(const Sched& sched, SegState& ss, uint8_t* smem, int row_in_tile,
+// Dequantizer role: DQ_WARPS warps in two groups of 4 (one thread per weight row of the tile). The
+// groups take alternating k-blocks of the CTA's k-block sequence, so two weight tiles are decoded
+// at once; a thread decodes its row's whole k-block (64 weights). Both groups read every raw
+// super-block stage and each warp releases it once.
+template <int FMT, bool BF16, int BT>
+__device__ __forceinline__ void dequant_role(const Sched& sched, SegState& ss, uint8_t* smem, int row_in_tile, int grp,
                                              const WView& w, uint32_t* err, bool& ok, uint32_t bar0, int lane) {
     using L = Smem<FMT, BT>;
-    constexpr int S = L::S, R = L::R;
-    auto full_a = [&](int s) { return bar0 + 8u * (S + s); };
-    auto empty = [&](int s) { return bar0 + 8u * (2 * S + s); };
-    auto raw_full = [&](int r) { return bar0 + 8u * (3 * S + r); };
-    auto raw_empty = [&](int r) { return bar0 + 8u * (3 * S + R + r); };
+    constexpr int SA = L::SA, R = L::R;
+    auto full_a = [&](int s) { return bar0 + 8u * (L::bar_full_a + s); };
+    auto empty_a = [&](int s) { return bar0 + 8u * (L::bar_empty_a + s); };
+    auto raw_full = [&](int r) { return bar0 + 8u * (L::bar_raw_full + r); };
+    auto raw_empty = [&](int r) { return bar0 + 8u * (L::bar_raw_empty + r); };
     const int sw = row_in_tile & 7;
-    SbDequant<FMT, BF16, PART> dq;
+    SbDequant<FMT, BF16> dq;
     int it = 0, raw_n = 0;
     Seg sg;
     while (ok && seg_next(sched, ss, sg)) {
@@ -377,22 +415,25 @@ __device__ __forceinline__ void dequant_role(const Sched& sched, SegState& ss, u
             for (int j = 0; j < 4; ++j) {
                 const int kb = 4 * sb + j;
                 if (kb < sg.kb_lo || kb >= sg.kb_hi) continue;
-                const int s = it % S;
-                if (it >= S) ok = __all_sync(0xFFFFFFFFu, mbar_wait(empty(s), ((it / S) - 1) & 1, err));
+                const int my = (it & 1) == grp;
+                const int s = it % SA;
+                ++it;
+                if (!my) continue;
+                const int it0 = it - 1;
+                if (it0 >= SA) ok = __all_sync(0xFFFFFFFFu, mbar_wait(empty_a(s), ((it0 / SA) - 1) & 1, err));
                 if (!ok) break;
-                JK_TRACE_POINT(6, it);
+                JK_TRACE_POINT(6, it0);
                 uint8_t* arow = smem + L::off_a + s * A_STAGE_BYTES + row_in_tile * 128;
                 switch (j) {
-                case 0: dq.template kblock<0>(raw_row, row_in_tile, arow, sw); break;
-                case 1: dq.template kblock<1>(raw_row, row_in_tile, arow, sw); break;
-                case 2: dq.template kblock<2>(raw_row, row_in_tile, arow, sw); break;
-                default: dq.template kblock<3>(raw_row, row_in_tile, arow, sw); break;
+                case 0: dq.template kblock<0, 0>(raw_row, row_in_tile, arow, sw); dq.template kblock<0, 1>(raw_row, row_in_tile, arow, sw); break;
+                case 1: dq.template kblock<1, 0>(raw_row, row_in_tile, arow, sw); dq.template kblock<1, 1>(raw_row, row_in_tile, arow, sw); break;
+                case 2: dq.template kblock<2, 0>(raw_row, row_in_tile, arow, sw); dq.template kblock<2, 1>(raw_row, row_in_tile, arow, sw); break;
+                default: dq.template kblock<3, 0>(raw_row, row_in_tile, arow, sw); dq.template kblock<3, 1>(raw_row, row_in_tile, arow, sw); break;
                 }
                 fence_proxy_async_smem();
                 __syncwarp();
-                JK_TRACE_POINT(9, it);
+                JK_TRACE_POINT(9, it0);
                 if (lane == 0) mbar_arrive(full_a(s));
-                ++it;
             }
             if (!ok) break;
             __syncwarp();
@@ -407,7 +448,7 @@ gemm_tc_kernel(const __grid_constant__ CUtensorMap tm_x, const __grid_constant__
                float* __restrict__ out, int64_t m, int64_t ldo, Sched sched, float* __restrict__ ws_part,
                uint32_t* __restrict__ ws_flag, uint32_t* err) {
     using L = Smem<FMT, BT>;
-    constexpr int S = L::S;
+    constexpr int SX = L::SX, SA = L::SA;
     constexpr bool QUANT = FMT != FMT_F16;
     constexpr uint32_t TMEM_COLS = 2 * BT;
     constexpr uint32_t IDESC = idesc_f16(BF16, BW, BT);
@@ -416,15 +457,16 @@ gemm_tc_kernel(const __grid_constant__ CUtensorMap tm_x, const __grid_constant__
     uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
     const uint32_t sbase = smem_u32(smem);
     const uint32_t bar0 = sbase + L::off_bar;
-    auto full_b = [&](int s) { return bar0 + 8u * s; };
-    auto full_a = [&](int s) { return bar0 + 8u * (S + s); };
-    auto empty = [&](int s) { return bar0 + 8u * (2 * S + s); };
+    auto full_b = [&](int s) { return bar0 + 8u * (L::bar_full_b + s); };
+    auto empty_b = [&](int s) { return bar0 + 8u * (L::bar_empty_b + s); };
+    auto full_a = [&](int s) { return bar0 + 8u * (L::bar_full_a + s); };
+    auto empty_a = [&](int s) { return bar0 + 8u * (L::bar_empty_a + s); };
     constexpr int R = L::R;
-    auto raw_full = [&](int r) { return bar0 + 8u * (3 * S + r); };
-    auto raw_empty = [&](int r) { return bar0 + 8u * (3 * S + R + r); };
-    auto acc_full = [&](int b) { return bar0 + 8u * (3 * S + 2 * R + b); };
-    auto acc_empty = [&](int b) { return bar0 + 8u * (3 * S + 2 * R + 2 + b); };
-    auto fix_full = [&](int i) { return bar0 + 8u * (3 * S + 2 * R + 4 + i); };
+    auto raw_full = [&](int r) { return bar0 + 8u * (L::bar_raw_full + r); };
+    auto raw_empty = [&](int r) { return bar0 + 8u * (L::bar_raw_empty + r); };
+    auto acc_full = [&](int b) { return bar0 + 8u * (L::bar_acc_full + b); };
+    auto acc_empty = [&](int b) { return bar0 + 8u * (L::bar_acc_empty + b); };
+    auto fix_full = [&](int i) { return bar0 + 8u * (L::bar_fix + i); };
     uint32_t* tmem_holder = reinterpret_cast<uint32_t*>(smem + L::off_tmem);
 
     const int warp = threadIdx.x >> 5;
@@ -432,10 +474,13 @@ gemm_tc_kernel(const __grid_constant__ CUtensorMap tm_x, const __grid_constant__
     const int cta = blockIdx.x;
 
     if (threadIdx.x == 0) {
-        for (int s = 0; s < S; ++s) {
+        for (int s = 0; s < SX; ++s) {
             mbar_init(full_b(s), 1);
-            mbar_init(full_a(s), DQ_WARPS);
-            mbar_init(empty(s), 1);
+            mbar_init(empty_b(s), 1);
+        }
+        for (int s = 0; s < SA; ++s) {
+            mbar_init(full_a(s), DQ_WARPS / 2);  // one group of dequantizer warps per k-block
+            mbar_init(empty_a(s), 1);
         }
         for (int r = 0; r < R; ++r) {
             mbar_init(raw_full(r), 1);
@@ -478,8 +523,8 @@ gemm_tc_kernel(const __grid_constant__ CUtensorMap tm_x, const __grid_constant__
             const int32_t n0 = (int32_t)((sg.tile / sched.tiles_m) * BW);
             const int32_t m0 = (int32_t)((sg.tile % sched.tiles_m) * BT);
             for (int kb = sg.kb_lo; kb < sg.kb_hi && ok; ++kb) {
-                const int s = it % S;
-                if (it >= S) ok = __all_sync(0xFFFFFFFFu, mbar_wait(empty(s), ((it / S) - 1) & 1, err));
+                const int s = it % SX;
+                if (it >= SX) ok = __all_sync(0xFFFFFFFFu, mbar_wait(empty_b(s), ((it / SX) - 1) & 1, err));
                 if (!ok) break;
                 JK_TRACE_POINT(1, it);
                 if (leader) {
@@ -496,7 +541,7 @@ gemm_tc_kernel(const __grid_constant__ CUtensorMap tm_x, const __grid_constant__
             }
         }
         if (!ok)  // drain: every copy this warp issued lands before the CTA may exit
-            for (int i = it - S < 0 ? 0 : it - S; i < it; ++i) mbar_wait(full_b(i % S), (i / S) & 1, err);
+            for (int i = it - SX < 0 ? 0 : it - SX; i < it; ++i) mbar_wait(full_b(i % SX), (i / SX) & 1, err);
     } else if (warp == RAW_WARP) {
         // --------------------- raw weight producer: runs up to R super-blocks ahead ---------------------
         if constexpr (QUANT) {
@@ -543,22 +588,22 @@ gemm_tc_kernel(const __grid_constant__ CUtensorMap tm_x, const __grid_constant__
             tc_fence_after();
             const uint32_t acc = tmem + (uint32_t)(b * BT);
             for (int kb = sg.kb_lo; kb < sg.kb_hi; ++kb, ++it) {
-                const int s = it % S;
-                const uint32_t ph = (it / S) & 1;
-                bool got = mbar_wait(full_b(s), ph, err);
+                const int sx = it % SX, sa = it % SA;
+                bool got = mbar_wait(full_b(sx), (uint32_t)((it / SX) & 1), err);
                 JK_TRACE_POINT(3, it);
-                if (got && QUANT) got = mbar_wait(full_a(s), ph, err);
+                if (got && QUANT) got = mbar_wait(full_a(sa), (uint32_t)((it / SA) & 1), err);
                 ok = __all_sync(0xFFFFFFFFu, got);
                 if (!ok) break;
                 JK_TRACE_POINT(4, it);
                 tc_fence_after();
-                const uint64_t ad = sw128_kmajor_desc(sbase + L::off_a + s * A_STAGE_BYTES);
-                const uint64_t bd = sw128_kmajor_desc(sbase + L::off_b + s * L::B_STAGE);
+                const uint64_t ad = sw128_kmajor_desc(sbase + L::off_a + sa * A_STAGE_BYTES);
+                const uint64_t bd = sw128_kmajor_desc(sbase + L::off_b + sx * L::B_STAGE);
                 if (leader) {
 #pragma unroll
                     for (int k = 0; k < KB / 16; ++k)  // +32 bytes per K=16 step inside the swizzle atom
                         mma_f16(acc, ad + 2u * k, bd + 2u * k, IDESC, (kb > sg.kb_lo || k > 0) ? 1u : 0u);
-                    mma_commit(empty(s));
+                    mma_commit(empty_b(sx));  // each commit arrives once these MMAs complete
+                    if constexpr (QUANT) mma_commit(empty_a(sa));
                 }
                 __syncwarp();
                 issued = true;
@@ -577,7 +622,7 @@ gemm_tc_kernel(const __grid_constant__ CUtensorMap tm_x, const __grid_constant__
             __syncwarp();
             mbar_wait(acc_full(b), (seg_i >> 1) & 1, err);
         }
-    } else if (warp < DQ_WARP0) {
+    } else if (warp >= EPI_WARP0 && warp < EPI_WARP0 + EPI_WARPS) {
         // ------------------------------ epilogue ------------------------------
         const int quarter = warp & 3;                 // TMEM lanes this warp may read
         const int row_in_tile = 32 * quarter + lane;  // weight row within the tile
@@ -756,13 +801,12 @@ gemm_tc_kernel(const __grid_constant__ CUtensorMap tm_x, const __grid_constant__
             if (lane == 0) mbar_arrive(acc_empty(b));
             ++seg_i;
         }
-    } else {
+    } else if (dq_slot(warp) >= 0) {
         // ------------------------------ dequantizers ------------------------------
         if constexpr (QUANT) {
-            const int t = threadIdx.x - 32 * DQ_WARP0;  // 0..255
+            const int t = 32 * dq_slot(warp) + lane;  // 0..255
             const int row_in_tile = t & (BW - 1);
-            if (t < BW) dequant_role<FMT, BF16, BT, 0>(sched, ss, smem, row_in_tile, w, err, ok, bar0, lane);
-            else dequant_role<FMT, BF16, BT, 1>(sched, ss, smem, row_in_tile, w, err, ok, bar0, lane);
+            dequant_role<FMT, BF16, BT>(sched, ss, smem, row_in_tile, t / BW, w, err, ok, bar0, lane);
         }
     }
 

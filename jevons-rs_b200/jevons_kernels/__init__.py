@@ -6,6 +6,7 @@ Python mirror of the reference's matmul path API over the C ABI in include/jk.h:
   * `gemm`     -- jevons-kernels: Gpu, Buf, QMatrix, Plan, SplitScratch, matmul, matmul_plan,
                   matvec, matmul_tiled; jevons-burn: f16_linear, f16_linear_scaled
   * `synth`    -- seeded synthetic GGML weights and activations with the benchmark shapes
+  * `shard`    -- column sharding of a projection across ranks and the all-gather of its outputs
 """
 from ._lib import JkError, Plan, load  # noqa: F401
 from .formats import Packed, TensorType, block, pack, packed_words, q4k_scale_min  # noqa: F401

@@ -285,12 +285,14 @@ def run_ours(args):
 
     def timed(fn, steps, warmup, use_graph=True):
         """Warm-up, then `steps` runs of fn timed with CUDA events on the current stream (max over
-        ranks). Single-GPU runs replay fn from a CUDA graph so host launch overhead is not timed."""
+        ranks). fn is replayed from a CUDA graph (NCCL all-gathers included: every rank captures
+        the same sequence after the warm-up created the communicator) so host launch overhead is
+        not timed."""
         for _ in range(warmup):
             fn()
         torch.cuda.synchronize()
         run = fn
-        if use_graph and world == 1:
+        if use_graph:
             g = torch.cuda.CUDAGraph()
             with torch.cuda.graph(g):
                 fn()
@@ -394,7 +396,7 @@ def run_ours(args):
             "e2e": {"value": e2e_value, "unit": "TFLOP/s", "h2d_bytes_per_step": xh.numel() * 2,
                     "d2h_bytes_per_step": oh.numel() * 4},
             "gpu_launches": args.steps * L * launches_per_product,
-            "timing": "CUDA graph replay of each step (1 GPU), CUDA events, max over ranks",
+            "timing": "CUDA graph replay of each step, CUDA events, max over ranks",
             "clocks": sampler.report(),
             "cpu_baseline": cpu,
         }

@@ -98,6 +98,14 @@ jk_status jk_gpu_sync(void *stream);
  * a code there instead of hanging). Synchronises the device. *code = 0 when clean. */
 jk_status jk_device_error(int device, uint32_t *code);
 
+/* Caps the number of multiprocessors the products on `device` may occupy (0 = all of them, the
+ * default). A caller that runs communication kernels (NCCL) alongside the products, as the
+ * column-sharded multi-GPU layout does, leaves SMs free for them with this so both overlap.
+ * Launches made after the call use the new cap. No counterpart in the reference (one device). */
+jk_status jk_set_max_ctas(int device, int max_sms);
+/* The cap set by jk_set_max_ctas (0 = none) and the device's SM count. */
+jk_status jk_get_max_ctas(int device, int *max_sms, int *sm_total);
+
 /* ---- quantized weight matrices -------------------------------------------------------------- */
 
 typedef struct jk_qmatrix jk_qmatrix;

@@ -16,6 +16,7 @@
 #include <algorithm>
 #include <cstdio>
 #include <cstring>
+#include <atomic>
 #include <mutex>
 #include <new>
 #include <thread>
@@ -193,6 +194,15 @@ int sm_count(int device) {
     return counts[device];
 }
 
+static std::atomic<int> g_sm_cap[MAX_DEVICES];
+
+int sm_budget(int device) {
+    const int total = sm_count(device);
+    if (device < 0 || device >= MAX_DEVICES) return total;
+    const int cap = g_sm_cap[device].load(std::memory_order_relaxed);
+    return cap > 0 && cap < total ? cap : total;
+}
+
 jk_status encode_tmap_2d(CUtensorMap* map, CUtensorMapDataType dt, uint64_t dim0, uint64_t dim1,
                          uint64_t stride1_bytes, uint32_t box0, uint32_t box1, CUtensorMapSwizzle swizzle,
                          const void* base) {
@@ -232,6 +242,20 @@ using jk::cuda_fail;
 // ================================================================================================
 extern "C" const char* jk_last_error(void) { return g_last_error.c_str(); }
 extern "C" int jk_abi_version(void) { return JK_ABI_VERSION; }
+
+extern "C" jk_status jk_set_max_ctas(int device, int max_sms) {
+    if (device < 0 || device >= MAX_DEVICES) return fail(JK_ERR_INVALID, "device index out of range");
+    if (max_sms < 0) return fail(JK_ERR_INVALID, "max_sms must be >= 0");
+    jk::g_sm_cap[device].store(max_sms, std::memory_order_relaxed);
+    return JK_OK;
+}
+
+extern "C" jk_status jk_get_max_ctas(int device, int* max_sms, int* sm_total) {
+    if (device < 0 || device >= MAX_DEVICES) return fail(JK_ERR_INVALID, "device index out of range");
+    if (max_sms) *max_sms = jk::g_sm_cap[device].load(std::memory_order_relaxed);
+    if (sm_total) *sm_total = jk::sm_count(device);
+    return JK_OK;
+}
 
 // ================================================================================================
 // block formats (host)

@@ -861,7 +861,7 @@ jk_status launch_tc(const LaunchArgs& a) {
     s.tiles = ((w.rows + BW - 1) / BW) * s.tiles_m;
     s.kbt = (int)(w.k / KB);
     s.sk = a.stream_k ? 1 : 0;
-    int64_t g = (int64_t)sm_count(dev) * per_sm;
+    int64_t g = (int64_t)sm_budget(dev) * per_sm;
     if (a.grid_cap > 0 && g > a.grid_cap) g = a.grid_cap;
     const int64_t work = s.sk ? s.tiles * s.kbt : s.tiles;
     if (g > work) g = work;
@@ -968,7 +968,7 @@ jk_status launch_gemm_stream_k_fixed(const jk_qmatrix* w, const void* x, bool x_
     // the grid the stream-K schedule uses: one CTA per SM (every instantiation runs one per SM),
     // never more CTAs than (tile, k-block) iterations
     const int64_t tiles = ((w->view.rows + BW - 1) / BW) * (((int64_t)m + bt - 1) / bt);
-    int64_t g = sm_count(dev);
+    int64_t g = sm_budget(dev);
     if (g > tiles * (w->k / KB)) g = tiles * (w->k / KB);
     if (g > max_ctas) {
         char buf[200];

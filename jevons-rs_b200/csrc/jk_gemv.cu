@@ -529,7 +529,7 @@ jk_status launch_gemv_t(const WView& w, const void* x, int x_dtype, int mrows, f
                         cudaStream_t stream) {
     int dev = 0;
     cudaGetDevice(&dev);
-    const int sms = sm_count(dev);
+    const int sms = sm_budget(dev);
     Geo geo{};
     geo.k = w.k;
     geo.steps = (w.k + 255) / 256;

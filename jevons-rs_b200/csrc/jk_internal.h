@@ -41,6 +41,8 @@ uint32_t* device_error_word(int device);
 
 // Multiprocessor count of `device` (cached).
 int sm_count(int device);
+// SMs the products may occupy on `device`: sm_count, or the jk_set_max_ctas cap when smaller.
+int sm_budget(int device);
 
 // cuTensorMapEncodeTiled through the runtime's driver entry point (no libcuda link needed).
 jk_status encode_tmap_2d(CUtensorMap* map, CUtensorMapDataType dt, uint64_t dim0, uint64_t dim1,

@@ -57,6 +57,8 @@ SIGNATURES = {
     "jk_matmul_tiled": (I, [P, P, I, S, S, P, S, I, I, P]),
     "jk_f16_linear": (I, [P, S, S, P, S, P, P]),
     "jk_matmul_splitk_noalloc": (I, [P, P, I, S, S, P, S, I, P]),
+    "jk_set_max_ctas": (I, [I, I]),
+    "jk_get_max_ctas": (I, [I, ctypes.POINTER(I), ctypes.POINTER(I)]),
 }
 
 STATUS = {0: "JK_OK", 1: "JK_ERR_INVALID", 2: "JK_ERR_UNSUPPORTED", 3: "JK_ERR_SHAPE", 4: "JK_ERR_CUDA",

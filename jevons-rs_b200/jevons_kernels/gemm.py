@@ -252,6 +252,19 @@ def matmul_tiled(gpu: Gpu, x: Buf, m: int, w: QMatrix, out: Buf, dummy=None, bm:
     check(load().jk_matmul_tiled(w.handle, xp, xt, xl, m, op, ol, bm, bn, _stream()))
 
 
+def set_max_ctas(gpu: Gpu, max_sms: int) -> None:
+    """Caps the SMs the products on gpu's device may occupy (0 = all). A multi-GPU caller leaves
+    SMs free for its communication kernels with this (jk_set_max_ctas)."""
+    check(load().jk_set_max_ctas(gpu.device, int(max_sms)))
+
+
+def get_max_ctas(gpu: Gpu) -> tuple[int, int]:
+    """(cap, SM count) of gpu's device; cap 0 = no cap."""
+    cap, total = ctypes.c_int(), ctypes.c_int()
+    check(load().jk_get_max_ctas(gpu.device, ctypes.byref(cap), ctypes.byref(total)))
+    return cap.value, total.value
+
+
 def matvec(gpu: Gpu, x: Buf, m: int, w: QMatrix, out: Buf, dummy=None) -> None:
     """matvec (gemm.rs:1135-1168): m <= GEMV_ROWS."""
     xp, xt, xl, op, ol = _args(x, out)

@@ -241,3 +241,27 @@ def test_stream_k_fixup_shapes(gpu, name, n, k, m):
                 if shift:
                     assert torch.isnan(big[0]).item()
     assert gpu.device_error() == 0
+
+
+def test_sm_cap_keeps_products_correct(gpu):
+    """jk_set_max_ctas: products launched under a cap (stream-K, whole tiles, small-row kernel)
+    stay within tolerance; the cap is per device and 0 lifts it."""
+    from jevons_kernels.gemm import Buf, Plan, SplitScratch, get_max_ctas, matmul_plan, matvec, set_max_ctas
+    w, _, dense = make_weights(gpu, KINDS["Q4_K"], 2560, 2560, seed=3)
+    scratch = SplitScratch(gpu)
+    try:
+        for cap in (37, 132, 0):
+            set_max_ctas(gpu, cap)
+            assert get_max_ctas(gpu)[0] == cap
+            for m, plan in ((256, Plan(256, 128, 2)), (96, Plan(128, 128, 1))):
+                x, x_exact = activations(m, 2560, torch.bfloat16, seed=m + cap)
+                out = torch.full((m, 2560), float("nan"), device="cuda")
+                matmul_plan(gpu, Buf(x), m, w, Buf(out), None, scratch, plan)
+                assert_close(f"cap {cap} m={m} {plan}", out.cpu().numpy(), x_exact, dense)
+            x, x_exact = activations(1, 2560, torch.bfloat16, seed=cap)
+            out = torch.full((1, 2560), float("nan"), device="cuda")
+            matvec(gpu, Buf(x), 1, w, Buf(out))
+            assert_close(f"cap {cap} gemv", out.cpu().numpy(), x_exact, dense)
+    finally:
+        set_max_ctas(gpu, 0)
+    assert gpu.device_error() == 0

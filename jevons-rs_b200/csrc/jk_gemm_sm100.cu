@@ -248,9 +248,49 @@ __device__ __forceinline__ void q4k_vals(uint32_t w0, uint32_t w1, float dd, flo
 template <int FMT, bool BF16>
 struct SbDequant;
 
+// Packed 16-bit arithmetic for the operand tiles: x2 = two bf16 (BF16) or two f16 values.
+template <bool BF16>
+__device__ __forceinline__ uint32_t h2_sub(uint32_t a, uint32_t b) {
+    uint32_t r;
+    if constexpr (BF16) asm("sub.rn.bf16x2 %0, %1, %2;" : "=r"(r) : "r"(a), "r"(b));
+    else asm("sub.rn.f16x2 %0, %1, %2;" : "=r"(r) : "r"(a), "r"(b));
+    return r;
+}
+template <bool BF16>
+__device__ __forceinline__ uint32_t h2_fma(uint32_t a, uint32_t b, uint32_t c) {
+    uint32_t r;
+    if constexpr (BF16) asm("fma.rn.bf16x2 %0, %1, %2, %3;" : "=r"(r) : "r"(a), "r"(b), "r"(c));
+    else asm("fma.rn.f16x2 %0, %1, %2, %3;" : "=r"(r) : "r"(a), "r"(b), "r"(c));
+    return r;
+}
+// Exponent byte of the 16-bit magic M (bf16 0x4300 = 128, f16 0x6400 = 1024): a byte b < 128
+// placed in the low byte gives the value M + b exactly. (Only the bf16 form is used for Q4_K.)
+template <bool BF16>
+constexpr uint32_t H2_MAGIC_HI = BF16 ? 0x43434343u : 0x64646464u;
+template <bool BF16>
+constexpr uint32_t H2_MAGIC = BF16 ? 0x43004300u : 0x64006400u;
+
+// Q4_K: 8 weights (the nibble bytes of w0, w1 -- each byte one 4-bit quant) as bf16/f16, packed in
+// k order. q is recovered exactly ((M + q) - M), then w = q * dd - mm in one rounding, with dd =
+// d*sc and mm = dmin*m rounded to the operand type: the error is within two roundings of the
+// 16-bit result (the per-element product tolerance covers it; jk_qmatrix_dequantize stays exact).
+template <bool BF16>
+__device__ __forceinline__ uint4 q4k_pack8(uint32_t w0, uint32_t w1, uint32_t dd2, uint32_t nmm2) {
+    constexpr uint32_t HI = H2_MAGIC_HI<BF16>, M = H2_MAGIC<BF16>;
+    uint4 r;
+    r.x = h2_fma<BF16>(h2_sub<BF16>(__byte_perm(w0, HI, 0x4140), M), dd2, nmm2);
+    r.y = h2_fma<BF16>(h2_sub<BF16>(__byte_perm(w0, HI, 0x4342), M), dd2, nmm2);
+    r.z = h2_fma<BF16>(h2_sub<BF16>(__byte_perm(w1, HI, 0x4140), M), dd2, nmm2);
+    r.w = h2_fma<BF16>(h2_sub<BF16>(__byte_perm(w1, HI, 0x4342), M), dd2, nmm2);
+    return r;
+}
+
+// bf16 operands: packed 16-bit decode (q4k_pack8). FP16 operands keep the exact f32 decode
+// rounded once: f16's range could overflow d*sc on its own where the f32 product does not.
 template <bool BF16>
 struct SbDequant<FMT_Q4K, BF16> {
-    float dd[8], mm[8];
+    uint32_t dd2[8], nmm2[8];  // bf16: (d*sc, d*sc) and (-dmin*m, -dmin*m) pairs per sub-block
+    float dd[8], mm[8];        // f16: exact f32 scale and min
     __device__ __forceinline__ void prefetch(const WView&, int64_t, int) {}
     __device__ __forceinline__ void begin(const uint8_t* raw_row, const WView&, int64_t, bool, int) {
         const uint4 hdr = *reinterpret_cast<const uint4*>(raw_row);
@@ -260,22 +300,40 @@ struct SbDequant<FMT_Q4K, BF16> {
         for (int j = 0; j < 8; ++j) {
             uint32_t sc, mn;
             q4k_scale_min(hdr.y, hdr.z, hdr.w, j, sc, mn);  // j is a compile-time constant here
-            dd[j] = __fmul_rn(d, (float)sc);
-            mm[j] = __fmul_rn(dmin, (float)mn);
+            const float a = __fmul_rn(d, (float)sc), b = __fmul_rn(dmin, (float)mn);
+            if constexpr (BF16) {
+                dd2[j] = pack2<true>(a, a);
+                nmm2[j] = pack2<true>(-b, -b);
+            } else {
+                dd[j] = a;
+                mm[j] = b;
+            }
         }
     }
     template <int J, int PART>
     __device__ __forceinline__ void kblock(const uint8_t* raw_row, int, uint8_t* arow, int sw) {
         const uint4 q = *reinterpret_cast<const uint4*>(raw_row + 16 + 32 * J + 16 * PART);
-        float v[8];
-        q4k_vals(q.x & 0x0F0F0F0Fu, q.y & 0x0F0F0F0Fu, dd[2 * J], mm[2 * J], v);
-        store_chunk8<BF16>(arow, sw, 2 * PART, v);
-        q4k_vals(q.z & 0x0F0F0F0Fu, q.w & 0x0F0F0F0Fu, dd[2 * J], mm[2 * J], v);
-        store_chunk8<BF16>(arow, sw, 2 * PART + 1, v);
-        q4k_vals((q.x >> 4) & 0x0F0F0F0Fu, (q.y >> 4) & 0x0F0F0F0Fu, dd[2 * J + 1], mm[2 * J + 1], v);
-        store_chunk8<BF16>(arow, sw, 2 * PART + 4, v);
-        q4k_vals((q.z >> 4) & 0x0F0F0F0Fu, (q.w >> 4) & 0x0F0F0F0Fu, dd[2 * J + 1], mm[2 * J + 1], v);
-        store_chunk8<BF16>(arow, sw, 2 * PART + 5, v);
+        if constexpr (BF16) {
+            const uint32_t dlo = dd2[2 * J], mlo = nmm2[2 * J], dhi = dd2[2 * J + 1], mhi = nmm2[2 * J + 1];
+            *reinterpret_cast<uint4*>(arow + 16 * ((2 * PART) ^ sw)) =
+                q4k_pack8<true>(q.x & 0x0F0F0F0Fu, q.y & 0x0F0F0F0Fu, dlo, mlo);
+            *reinterpret_cast<uint4*>(arow + 16 * ((2 * PART + 1) ^ sw)) =
+                q4k_pack8<true>(q.z & 0x0F0F0F0Fu, q.w & 0x0F0F0F0Fu, dlo, mlo);
+            *reinterpret_cast<uint4*>(arow + 16 * ((2 * PART + 4) ^ sw)) =
+                q4k_pack8<true>((q.x >> 4) & 0x0F0F0F0Fu, (q.y >> 4) & 0x0F0F0F0Fu, dhi, mhi);
+            *reinterpret_cast<uint4*>(arow + 16 * ((2 * PART + 5) ^ sw)) =
+                q4k_pack8<true>((q.z >> 4) & 0x0F0F0F0Fu, (q.w >> 4) & 0x0F0F0F0Fu, dhi, mhi);
+        } else {
+            float v[8];
+            q4k_vals(q.x & 0x0F0F0F0Fu, q.y & 0x0F0F0F0Fu, dd[2 * J], mm[2 * J], v);
+            store_chunk8<false>(arow, sw, 2 * PART, v);
+            q4k_vals(q.z & 0x0F0F0F0Fu, q.w & 0x0F0F0F0Fu, dd[2 * J], mm[2 * J], v);
+            store_chunk8<false>(arow, sw, 2 * PART + 1, v);
+            q4k_vals((q.x >> 4) & 0x0F0F0F0Fu, (q.y >> 4) & 0x0F0F0F0Fu, dd[2 * J + 1], mm[2 * J + 1], v);
+            store_chunk8<false>(arow, sw, 2 * PART + 4, v);
+            q4k_vals((q.z >> 4) & 0x0F0F0F0Fu, (q.w >> 4) & 0x0F0F0F0Fu, dd[2 * J + 1], mm[2 * J + 1], v);
+            store_chunk8<false>(arow, sw, 2 * PART + 5, v);
+        }
     }
 };
 

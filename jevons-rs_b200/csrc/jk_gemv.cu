@@ -49,13 +49,18 @@ constexpr int WARPS = 8;
 constexpr int THREADS = 32 * WARPS;
 constexpr int GROUP_ROWS = 8;         // weight rows per warp item (4 lanes per row)
 constexpr int SLOTS_PER_WARP = 2;
+#ifndef JK_GEMV_WARP_TARGET_OVERRIDE
+constexpr int WARP_TARGET = 1;        // K parts grow until row groups x parts >= SMs x WARPS x this
+#else
+constexpr int WARP_TARGET = JK_GEMV_WARP_TARGET_OVERRIDE;
+#endif
 constexpr int SLOT_WORDS = 40;        // per (step, lane) activation slot, 160 bytes
 // activation slot layout (words): [0,16) xq lo[32] int16 | [16,32) xq hi[32] | 32 s_lo | 33 s_hi |
 //                                 34..37 sums of xq over lo[0:16), lo[16:32), hi[0:16), hi[16:32) | pad
 
 // Per-launch geometry, computed on the host.
 struct Geo {
-    int64_t k, steps, rowgroups;
+    int k, steps, rowgroups;    // 32-bit: the host checks the matrix fits
     int P;                      // warps per row group
     int KS;                     // 256-weight steps per segment
     int qsb, dsb, hsb;          // bytes per 256 weights of q, d (f16 scales), h (Q5_0 high bits)
@@ -98,7 +103,7 @@ __device__ __forceinline__ int dot16(const uint32_t (&q)[4], const uint4& xa, co
 
 // Activation slot (step st, lane-in-row g, side h, 16-half) holding element e0 (a multiple of 16).
 template <int FMT>
-__device__ __forceinline__ void slot_of(int64_t e0, int64_t& st, int& g, int& h) {
+__device__ __forceinline__ void slot_of(int e0, int& st, int& g, int& h) {
     st = e0 >> 8;
     if constexpr (FMT == FMT_Q6K) {
         const int in_sb = (int)(e0 & 255);
@@ -149,17 +154,17 @@ __device__ __forceinline__ void load8(const void* x, int x_dtype, int64_t idx, b
 template <int FMT, int MR>
 __device__ __forceinline__ void stage_x(const Geo& geo, const void* x, int x_dtype, int mrows, uint32_t* xs) {
     constexpr int U = 4;
-    const int64_t kc = geo.k / 8;                 // chunks per row
-    const int64_t chunks = (int64_t)MR * kc;
-    const int64_t row_words = geo.steps * 4 * SLOT_WORDS;
-    for (int64_t c0 = 0; c0 < chunks; c0 += (int64_t)THREADS * U) {
+    const int kc = geo.k / 8;                 // chunks per row
+    const int chunks = (int)MR * kc;
+    const int row_words = geo.steps * 4 * SLOT_WORDS;
+    for (int c0 = 0; c0 < chunks; c0 += (int)THREADS * U) {
         float v[U][8];
 #pragma unroll
         for (int u = 0; u < U; ++u) {
-            const int64_t c = c0 + (int64_t)u * THREADS + threadIdx.x;
-            const int64_t r = c / kc;
+            const int c = c0 + u * THREADS + threadIdx.x;
+            const int r = MR == 1 ? 0 : c / kc;
             if (c < chunks && r < mrows) {
-                load8(x, x_dtype, r * geo.k + (c - r * kc) * 8, geo.x_vec != 0, v[u]);
+                load8(x, x_dtype, (int64_t)r * geo.k + (c - r * kc) * 8, geo.x_vec != 0, v[u]);
             } else {
 #pragma unroll
                 for (int i = 0; i < 8; ++i) v[u][i] = 0.f;
@@ -167,7 +172,8 @@ __device__ __forceinline__ void stage_x(const Geo& geo, const void* x, int x_dty
         }
 #pragma unroll
         for (int u = 0; u < U; ++u) {
-            const int64_t c = c0 + (int64_t)u * THREADS + threadIdx.x;
+            if (c0 + u * THREADS >= chunks) break;  // block-uniform: no lane of this pass has a chunk
+            const int c = c0 + u * THREADS + threadIdx.x;
             float amax = 0.f;
 #pragma unroll
             for (int i = 0; i < 8; ++i) amax = fmaxf(amax, fabsf(v[u][i]));
@@ -185,11 +191,11 @@ __device__ __forceinline__ void stage_x(const Geo& geo, const void* x, int x_dty
             }
             const int sum16 = sum + __shfl_xor_sync(0xFFFFFFFFu, sum, 1);
             if (c < chunks) {
-                const int64_t r = c / kc;
-                const int64_t e0 = (c - r * kc) * 8;
-                int64_t st;
+                const int r = MR == 1 ? 0 : c / kc;
+                const int e0 = (c - r * kc) * 8;
+                int st;
                 int g, h;
-                slot_of<FMT>(e0 & ~(int64_t)15, st, g, h);
+                slot_of<FMT>(e0 & ~15, st, g, h);
                 const int half16 = (int)((e0 >> 4) & 1), sub8 = (int)((e0 >> 3) & 1);
                 uint32_t* sl = xs + r * row_words + (st * 4 + g) * SLOT_WORDS;
                 *reinterpret_cast<uint4*>(sl + 16 * h + 8 * half16 + 4 * sub8) =
@@ -212,21 +218,22 @@ __global__ void __launch_bounds__(THREADS, MR <= 2 ? 2 : 1) gemv_kernel(WView w,
     uint8_t* slots = smem + 4 * (size_t)geo.x_words + 4 * (size_t)geo.red_floats;
 
     pdl_trigger();  // the next product may start its weight stream as soon as it fits on an SM
+    JK_TRACE_POINT(1, 0);
 
     const int lane = threadIdx.x & 31;
     const int warp = threadIdx.x >> 5;
     const int P = geo.P;
     const int grp = warp / P, part = warp % P;
     const int per_iter = WARPS / P;
-    const int64_t st_lo = (int64_t)part * geo.steps / P, st_hi = (int64_t)(part + 1) * geo.steps / P;
+    const int st_lo = (int)part * geo.steps / P, st_hi = (int)(part + 1) * geo.steps / P;
     const int nseg = (int)((st_hi - st_lo + geo.KS - 1) / geo.KS);
-    const int64_t first = (int64_t)blockIdx.x * per_iter + grp;
-    const int64_t stride = (int64_t)gridDim.x * per_iter;
-    const int64_t kg = first < geo.rowgroups ? (geo.rowgroups - 1 - first) / stride + 1 : 0;
-    const int64_t items = kg * nseg;
+    const int first = (int)blockIdx.x * per_iter + grp;
+    const int stride = (int)gridDim.x * per_iter;
+    const int kg = first < geo.rowgroups ? (geo.rowgroups - 1 - first) / stride + 1 : 0;
+    const int items = kg * nseg;
     // all warps of the CTA run the same number of row-group iterations (group barriers)
-    const int64_t k_cta = ((int64_t)blockIdx.x * per_iter < geo.rowgroups)
-                              ? (geo.rowgroups - 1 - (int64_t)blockIdx.x * per_iter) / stride + 1 : 0;
+    const int k_cta = ((int)blockIdx.x * per_iter < geo.rowgroups)
+                              ? (geo.rowgroups - 1 - (int)blockIdx.x * per_iter) / stride + 1 : 0;
 
     const uint32_t bar0 = smem_u32(&bars[warp * SLOTS_PER_WARP]);
     const uint32_t slot0 = smem_u32(slots) + (uint32_t)(warp * SLOTS_PER_WARP) * (uint32_t)geo.slot_bytes;
@@ -238,29 +245,29 @@ __global__ void __launch_bounds__(THREADS, MR <= 2 ? 2 : 1) gemv_kernel(WView w,
 
     // Copies of item i into slot i % 2: row segment bytes of q, then the d / h words covering it
     // (rounded out to 16-byte boundaries; allocations carry the slack).
-    auto issue = [&](int64_t i) {
-        const int64_t kk = i / nseg;
+    auto issue = [&](int i) {
+        const int kk = i / nseg;
         const int s = (int)(i - kk * nseg);
-        const int64_t rg = first + kk * stride;
-        const int64_t st0 = st_lo + (int64_t)s * geo.KS;
-        const int64_t st1 = st0 + geo.KS < st_hi ? st0 + geo.KS : st_hi;
-        const int64_t e0 = st0 * 256, e1 = st1 * 256 < geo.k ? st1 * 256 : geo.k;
+        const int rg = first + kk * stride;
+        const int st0 = st_lo + (int)s * geo.KS;
+        const int st1 = st0 + geo.KS < st_hi ? st0 + geo.KS : st_hi;
+        const int e0 = st0 * 256, e1 = st1 * 256 < geo.k ? st1 * 256 : geo.k;
         const uint32_t slot = slot0 + (uint32_t)(i & 1) * (uint32_t)geo.slot_bytes;
         const uint32_t bar = bar0 + 8u * (uint32_t)(i & 1);
         uint32_t bytes = 0, qb = 0, db = 0, hb = 0;
         const uint8_t *qs = nullptr, *ds = nullptr, *hs = nullptr;
         if (lane < GROUP_ROWS) {
-            const int64_t row = rg * GROUP_ROWS + lane;
-            qs = w.q + row * w.q_row_bytes + e0 * geo.qsb / 256;
+            const int row = rg * GROUP_ROWS + lane;
+            qs = w.q + (int64_t)row * w.q_row_bytes + (int64_t)e0 * geo.qsb / 256;
             qb = (uint32_t)((e1 - e0) * geo.qsb / 256);
             if (geo.dsb) {
-                const uintptr_t a = reinterpret_cast<uintptr_t>(w.d) + row * geo.d_row_bytes + e0 * geo.dsb / 256;
+                const uintptr_t a = reinterpret_cast<uintptr_t>(w.d) + (int64_t)row * geo.d_row_bytes + (int64_t)e0 * geo.dsb / 256;
                 const uintptr_t b = a + (e1 - e0) * geo.dsb / 256;
                 ds = reinterpret_cast<const uint8_t*>(a & ~(uintptr_t)15);
                 db = (uint32_t)(((b + 15) & ~(uintptr_t)15) - (a & ~(uintptr_t)15));
             }
             if (geo.hsb) {
-                const uintptr_t a = reinterpret_cast<uintptr_t>(w.h) + row * geo.h_row_bytes + e0 * geo.hsb / 256;
+                const uintptr_t a = reinterpret_cast<uintptr_t>(w.h) + (int64_t)row * geo.h_row_bytes + (int64_t)e0 * geo.hsb / 256;
                 const uintptr_t b = a + (e1 - e0) * geo.hsb / 256;
                 hs = reinterpret_cast<const uint8_t*>(a & ~(uintptr_t)15);
                 hb = (uint32_t)(((b + 15) & ~(uintptr_t)15) - (a & ~(uintptr_t)15));
@@ -280,20 +287,23 @@ __global__ void __launch_bounds__(THREADS, MR <= 2 ? 2 : 1) gemv_kernel(WView w,
 
     if (items > 0) issue(0);
     if (items > 1) issue(1);
+    JK_TRACE_POINT(2, 0);
 
     pdl_wait();  // activations come from the previous grid; outputs may be read by it
+    JK_TRACE_POINT(3, 0);
     stage_x<FMT, MR>(geo, x, x_dtype, mrows, xs);
     __syncthreads();
+    JK_TRACE_POINT(4, 0);
 
     const int g = lane & 3;       // lane within the row
     const int rsub = lane >> 2;   // row within the group
-    const int64_t row_words = geo.steps * 4 * SLOT_WORDS;
+    const int row_words = geo.steps * 4 * SLOT_WORDS;
     const bool upper = g >= 2;    // Q4_K: this lane's sub-blocks are 2g and 2g+1
     const int jj = (2 * g) & 3;
     bool ok = true;
-    int64_t i = 0;
+    int i = 0;
 
-    for (int64_t kk = 0; kk < k_cta; ++kk) {
+    for (int kk = 0; kk < k_cta; ++kk) {
         const bool live = kk < kg;
         float acc[MR];
 #pragma unroll
@@ -301,24 +311,25 @@ __global__ void __launch_bounds__(THREADS, MR <= 2 ? 2 : 1) gemv_kernel(WView w,
         for (int s = 0; live && s < nseg; ++s, ++i) {
             if (ok) ok = __all_sync(0xFFFFFFFFu, mbar_wait(bar0 + 8u * (uint32_t)(i & 1), (uint32_t)((i >> 1) & 1), err));
             if (!ok) break;  // i stays at the item that did not arrive
+            JK_TRACE_POINT(5, i);
             const uint8_t* slot = slots + (size_t)(warp * SLOTS_PER_WARP + (int)(i & 1)) * geo.slot_bytes;
             const uint8_t* qrow = slot + rsub * geo.q_area;
-            const int64_t st0 = st_lo + (int64_t)s * geo.KS;
-            const int64_t st1 = st0 + geo.KS < st_hi ? st0 + geo.KS : st_hi;
-            const int64_t row = (first + kk * stride) * GROUP_ROWS + rsub;
+            const int st0 = st_lo + (int)s * geo.KS;
+            const int st1 = st0 + geo.KS < st_hi ? st0 + geo.KS : st_hi;
+            const int row = (first + kk * stride) * GROUP_ROWS + rsub;
             // start of this row's d / h words inside the slot (the copy began 16-byte aligned)
             const uint8_t* drow = nullptr;
             const uint8_t* hrow = nullptr;
             if (geo.dsb) {
-                const uintptr_t a = reinterpret_cast<uintptr_t>(w.d) + row * geo.d_row_bytes + st0 * 256 * geo.dsb / 256;
+                const uintptr_t a = reinterpret_cast<uintptr_t>(w.d) + (int64_t)row * geo.d_row_bytes + st0 * geo.dsb;
                 drow = slot + GROUP_ROWS * geo.q_area + rsub * geo.d_area + (a & 15);
             }
             if (geo.hsb) {
-                const uintptr_t a = reinterpret_cast<uintptr_t>(w.h) + row * geo.h_row_bytes + st0 * 256 * geo.hsb / 256;
+                const uintptr_t a = reinterpret_cast<uintptr_t>(w.h) + (int64_t)row * geo.h_row_bytes + st0 * geo.hsb;
                 hrow = slot + GROUP_ROWS * (geo.q_area + geo.d_area) + rsub * geo.h_area + (a & 15);
             }
 #pragma unroll 2
-            for (int64_t st = st0; st < st1; ++st) {
+            for (int st = st0; st < st1; ++st) {
                 const int sl = (int)(st - st0);
                 const uint32_t* sl0 = xs + (st * 4 + g) * SLOT_WORDS;
                 if constexpr (FMT == FMT_Q4K) {
@@ -394,7 +405,7 @@ __global__ void __launch_bounds__(THREADS, MR <= 2 ? 2 : 1) gemv_kernel(WView w,
                         acc[r] += sm.x * (s0 * a0 + s1 * a1) + sm.y * (s2 * a2 + s3 * a3);
                     }
                 } else if constexpr (FMT == FMT_Q8_0 || FMT == FMT_Q5_0) {
-                    const int64_t blk = 8 * st + 2 * g;  // this lane's two blocks
+                    const int blk = 8 * st + 2 * g;  // this lane's two blocks
                     if (blk < geo.k / 32) {
                         const int lb = 8 * sl + 2 * g;     // block index within the segment
                         uint32_t q0[4], q1[4], q2[4], q3[4];
@@ -444,7 +455,7 @@ __global__ void __launch_bounds__(THREADS, MR <= 2 ? 2 : 1) gemv_kernel(WView w,
                         }
                     }
                 } else {  // FMT_F16: f32 math on the half weights, x from the int16 slots
-                    const int64_t e0 = 256 * st + 64 * g;
+                    const int e0 = 256 * st + 64 * g;
                     if (e0 < geo.k) {
                         const uint8_t* p = qrow + 2 * (e0 - 256 * st0);
                         float wf[64];
@@ -477,6 +488,7 @@ __global__ void __launch_bounds__(THREADS, MR <= 2 ? 2 : 1) gemv_kernel(WView w,
                 }
             }
             // the slot's bytes are consumed: hand it to the async proxy for the item two ahead
+            JK_TRACE_POINT(6, i);
             __syncwarp();
             fence_proxy_async_smem();
             if (i + 2 < items) issue(i + 2);
@@ -489,12 +501,12 @@ __global__ void __launch_bounds__(THREADS, MR <= 2 ? 2 : 1) gemv_kernel(WView w,
             v += __shfl_xor_sync(0xFFFFFFFFu, v, 2);
             acc[r] = v;
         }
-        const int64_t row = (first + kk * stride) * GROUP_ROWS + rsub;
+        const int row = (first + kk * stride) * GROUP_ROWS + rsub;
         if (P == 1) {
             if (live && ok && g == 0) {
 #pragma unroll
                 for (int r = 0; r < MR; ++r)
-                    if (r < mrows) out[r * ldo + row] = acc[r];
+                    if (r < mrows) out[(int64_t)r * ldo + row] = acc[r];
             }
         } else {
             float* rb = red + (size_t)(kk & 1) * WARPS * MR * GROUP_ROWS;
@@ -508,14 +520,15 @@ __global__ void __launch_bounds__(THREADS, MR <= 2 ? 2 : 1) gemv_kernel(WView w,
                 for (int r = 0; r < MR; ++r) {
                     float v = 0.f;
                     for (int q = 0; q < P; ++q) v += rb[((warp + q) * MR + r) * GROUP_ROWS + rsub];
-                    if (r < mrows) out[r * ldo + row] = v;
+                    if (r < mrows) out[(int64_t)r * ldo + row] = v;
                 }
             }
         }
     }
+    JK_TRACE_POINT(7, 0);
     if (!ok) {
         // a wait gave up at item i: let this warp's copies still in flight land before exiting
-        for (int64_t j = i; j < items && j < i + SLOTS_PER_WARP; ++j)
+        for (int j = i; j < items && j < i + SLOTS_PER_WARP; ++j)
             (void)mbar_wait(bar0 + 8u * (uint32_t)(j & 1), (uint32_t)((j >> 1) & 1), err);
     }
 }
@@ -531,9 +544,11 @@ jk_status launch_gemv_t(const WView& w, const void* x, int x_dtype, int mrows, f
     cudaGetDevice(&dev);
     const int sms = sm_budget(dev);
     Geo geo{};
-    geo.k = w.k;
-    geo.steps = (w.k + 255) / 256;
-    geo.rowgroups = w.rows / GROUP_ROWS;
+    if (w.k > (1 << 30) || w.rows > (1 << 30) || (int64_t)MR * w.k / 8 > (1 << 30))
+        return fail(JK_ERR_UNSUPPORTED, "gemv: matrix too large for 32-bit indexing");
+    geo.k = (int)w.k;
+    geo.steps = (int)((w.k + 255) / 256);
+    geo.rowgroups = (int)(w.rows / GROUP_ROWS);
     switch (FMT) {
     case FMT_Q4K: geo.qsb = 144; break;
     case FMT_Q6K: geo.qsb = 208; geo.dsb = 2; break;
@@ -551,7 +566,8 @@ jk_status launch_gemv_t(const WView& w, const void* x, int x_dtype, int mrows, f
 
     // warps per row group: enough warp items for 8 warps per SM, never more parts than steps
     geo.P = 1;
-    while (geo.P < WARPS && geo.rowgroups * geo.P < (int64_t)sms * WARPS && 2 * geo.P <= geo.steps) geo.P *= 2;
+    while (geo.P < WARPS && (int64_t)geo.rowgroups * geo.P < (int64_t)sms * WARPS * WARP_TARGET && 2 * geo.P <= geo.steps)
+        geo.P *= 2;
     const int64_t steps_w = (geo.steps + geo.P - 1) / geo.P;
 
     // slot size: two CTAs per SM when the staged activations are small, else one

@@ -144,9 +144,11 @@ jk_status jk_qmatrix_dequantize(const jk_qmatrix *w, float *out_dev, size_t out_
 
 /* Plan (gemm.rs:973-1016). bm == 0 selects the small-row kernel (m <= JK_GEMV_ROWS).
  * Otherwise bm is the activation-row tile of the tensor-core kernel (MMA N: 32, 64, 128 or
- * 256), bn the weight-row tile (MMA M: 128) and splits the split-K factor (1..16). Plans with
- * bm > 0 and splits == 1 are row invariant: every output row is accumulated in the same order
- * whatever m or bm is (gemm.rs:1090-1091). */
+ * 256), bn the weight-row tile and splits the split-K factor (1..16). bn = 128 runs one CTA per
+ * tile (MMA M = 128); bn = 256 (block-quantized weights, bm >= 128) runs each tile on a pair of
+ * CTAs with one M = 256 MMA (tcgen05 cta_group::2), each CTA dequantizing 128 rows and loading
+ * half the activation rows. Plans with bm > 0 and splits == 1 are row invariant: every output row
+ * is accumulated in the same order whatever m, bm or bn is (gemm.rs:1090-1091). */
 typedef struct jk_plan {
     int32_t bm;
     int32_t bn;

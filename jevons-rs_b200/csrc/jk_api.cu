@@ -656,7 +656,11 @@ int choose_splits(size_t base, size_t steps, size_t target) {
 bool plan_valid(const jk_plan& p, const jk_qmatrix* w, size_t m) {
     if (p.bm == 0) return m <= JK_GEMV_ROWS && p.splits == 1 && w->k / 32 <= 1u << 20;
     const bool bm_ok = p.bm == 32 || p.bm == 64 || p.bm == 128 || p.bm == 256;
-    return bm_ok && p.bn == 128 && p.splits >= 1 && p.splits <= 16 && w->k / 64 >= (size_t)p.splits;
+    // bn: weight rows per tile. 128 = one CTA per tile; 256 = a CTA pair (tcgen05 cta_group::2,
+    // each CTA dequantizes 128 rows and loads half the activation rows) for block-quantized
+    // weights at bm >= 128.
+    const bool bn_ok = p.bn == 128 || (p.bn == 256 && w->type != JK_TYPE_F16 && p.bm >= 128);
+    return bm_ok && bn_ok && p.splits >= 1 && p.splits <= 16 && w->k / 64 >= (size_t)p.splits;
 }
 
 jk_status check_launch(const jk_qmatrix* w, const void* x, int x_dtype, size_t x_len, size_t m, const float* out,
@@ -809,7 +813,7 @@ extern "C" jk_status jk_matmul_plan(const jk_qmatrix* w, const void* x, int x_dt
     if ((reinterpret_cast<uintptr_t>(xk) & 15) != 0) return fail(JK_ERR_INVALID, "activations must be 16-byte aligned");
     jk_qmatrix dense = *w;
     dense.view = dense_view(w);
-    return jk::launch_gemm(&dense, xk, want_bf16, m, out, plan.bm, stream_k, sbuf, ws_bytes, cs);
+    return jk::launch_gemm(&dense, xk, want_bf16, m, out, plan.bm, plan.bn == 256, stream_k, sbuf, ws_bytes, cs);
 }
 
 extern "C" jk_status jk_matmul(const jk_qmatrix* w, const void* x, int x_dtype, size_t x_len, size_t m, float* out,

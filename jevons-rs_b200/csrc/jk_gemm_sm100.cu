@@ -94,9 +94,9 @@ constexpr Rings pick_rings(int b_stage, int raw_bytes) {
     return Rings{2, 2, 2};
 }
 
-template <int FMT, int BT>
+template <int FMT, int BT, bool PAIR = false>
 struct Smem {
-    static constexpr int B_STAGE = BT * 128;
+    static constexpr int B_STAGE = (PAIR ? BT / 2 : BT) * 128;  // a pair CTA holds half the activation rows
     static constexpr int raw_bytes = RawTile<FMT>::bytes;
     static constexpr Rings rings = pick_rings(B_STAGE, raw_bytes);
     static constexpr int SX = rings.sx, SA = rings.sa, R = rings.r;
@@ -173,6 +173,53 @@ __device__ __forceinline__ void bulk_commit() { asm volatile("cp.async.bulk.comm
 template <int N>
 __device__ __forceinline__ void bulk_wait_read() { asm volatile("cp.async.bulk.wait_group.read %0;" :: "n"(N) : "memory"); }
 __device__ __forceinline__ void bulk_wait_all() { asm volatile("cp.async.bulk.wait_group 0;" ::: "memory"); }
+
+// ---- CTA pairs (tcgen05 cta_group::2): the two CTAs of a cluster share one 256-row MMA ----
+__device__ __forceinline__ uint32_t cluster_ctarank() {
+    uint32_t r;
+    asm volatile("mov.u32 %0, %%cluster_ctarank;" : "=r"(r));
+    return r;
+}
+// the shared::cluster address of `addr` (a shared::cta address of this CTA's layout) in CTA `rank`
+__device__ __forceinline__ uint32_t mapa_shared(uint32_t addr, uint32_t rank) {
+    uint32_t r;
+    asm volatile("mapa.shared::cluster.u32 %0, %1, %2;" : "=r"(r) : "r"(addr), "r"(rank));
+    return r;
+}
+__device__ __forceinline__ void mbar_arrive_cluster(uint32_t cluster_addr) {
+    asm volatile("mbarrier.arrive.release.cluster.shared::cluster.b64 _, [%0];" :: "r"(cluster_addr) : "memory");
+}
+__device__ __forceinline__ void cluster_sync() {
+    asm volatile("barrier.cluster.arrive.release.aligned;\n\tbarrier.cluster.wait.acquire.aligned;" ::: "memory");
+}
+__device__ __forceinline__ void tmem_alloc_pair(uint32_t dst_smem, uint32_t ncols) {
+    asm volatile("tcgen05.alloc.cta_group::2.sync.aligned.shared::cta.b32 [%0], %1;" :: "r"(dst_smem), "r"(ncols) : "memory");
+}
+__device__ __forceinline__ void tmem_relinquish_pair() {
+    asm volatile("tcgen05.relinquish_alloc_permit.cta_group::2.sync.aligned;" ::: "memory");
+}
+__device__ __forceinline__ void tmem_dealloc_pair(uint32_t taddr, uint32_t ncols) {
+    asm volatile("tcgen05.dealloc.cta_group::2.sync.aligned.b32 %0, %1;" :: "r"(taddr), "r"(ncols) : "memory");
+}
+// D[tmem of both CTAs] (+)= A (128 rows from each CTA's smem) x B^T (N/2 rows from each CTA's smem)
+__device__ __forceinline__ void mma_f16_pair(uint32_t d_tmem, uint64_t a_desc, uint64_t b_desc, uint32_t idesc,
+                                             uint32_t accumulate) {
+    asm volatile(
+        "{ .reg .pred p; setp.ne.b32 p, %4, 0; tcgen05.mma.cta_group::2.kind::f16 [%0], %1, %2, %3, p; }"
+        :: "r"(d_tmem), "l"(a_desc), "l"(b_desc), "r"(idesc), "r"(accumulate) : "memory");
+}
+// arrive on the mbarrier at offset `bar` in both CTAs of the pair once the issued MMAs complete
+__device__ __forceinline__ void mma_commit_pair(uint32_t bar) {
+    asm volatile("tcgen05.commit.cta_group::2.mbarrier::arrive::one.shared::cluster.multicast::cluster.b64 [%0], %1;"
+                 :: "r"(bar), "h"((unsigned short)3) : "memory");
+}
+// this CTA's half of a pair operand tile; the transaction bytes count on the leader CTA's barrier
+__device__ __forceinline__ void tma_load_2d_pair(uint32_t dst, const CUtensorMap* m, int32_t c0, int32_t c1,
+                                                 uint32_t leader_bar) {
+    asm volatile(
+        "cp.async.bulk.tensor.2d.cta_group::2.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1, {%2, %3}], [%4];"
+        :: "r"(dst), "l"(m), "r"(c0), "r"(c1), "r"(leader_bar) : "memory");
+}
 
 __device__ __forceinline__ bool seg_next(const Sched& s, SegState& st, Seg& g) {
     if (st.next >= st.end) return false;
@@ -441,10 +488,11 @@ struct SbDequant<FMT_Q5_0, BF16> {
 // groups take alternating k-blocks of the CTA's k-block sequence, so two weight tiles are decoded
 // at once; a thread decodes its row's whole k-block (64 weights). Both groups read every raw
 // super-block stage and each warp releases it once.
-template <int FMT, bool BF16, int BT>
+template <int FMT, bool BF16, int BT, bool PAIR>
 __device__ __forceinline__ void dequant_role(const Sched& sched, SegState& ss, uint8_t* smem, int row_in_tile, int grp,
-                                             const WView& w, uint32_t* err, bool& ok, uint32_t bar0, int lane) {
-    using L = Smem<FMT, BT>;
+                                             int rank, const WView& w, uint32_t* err, bool& ok, uint32_t bar0, int lane) {
+    using L = Smem<FMT, BT, PAIR>;
+    constexpr int TW = PAIR ? 2 * BW : BW;  // weight rows per tile
     constexpr int SA = L::SA, R = L::R;
     auto full_a = [&](int s) { return bar0 + 8u * (L::bar_full_a + s); };
     auto empty_a = [&](int s) { return bar0 + 8u * (L::bar_empty_a + s); };
@@ -455,7 +503,7 @@ __device__ __forceinline__ void dequant_role(const Sched& sched, SegState& ss, u
     int it = 0, raw_n = 0;
     Seg sg;
     while (ok && seg_next(sched, ss, sg)) {
-        const int64_t row = (sg.tile / sched.tiles_m) * BW + row_in_tile;
+        const int64_t row = (sg.tile / sched.tiles_m) * TW + rank * BW + row_in_tile;
         const bool row_ok = row < w.rows;
         const int64_t rr = row_ok ? row : 0;
         const int sb_lo = sg.kb_lo >> 2, sb_hi = (sg.kb_hi - 1) >> 2;
@@ -491,7 +539,10 @@ __device__ __forceinline__ void dequant_role(const Sched& sched, SegState& ss, u
                 fence_proxy_async_smem();
                 __syncwarp();
                 JK_TRACE_POINT(9, it0);
-                if (lane == 0) mbar_arrive(full_a(s));
+                if (lane == 0) {
+                    if constexpr (PAIR) mbar_arrive_cluster(mapa_shared(full_a(s), 0));  // the leader issues the MMA
+                    else mbar_arrive(full_a(s));
+                }
             }
             if (!ok) break;
             __syncwarp();
@@ -500,16 +551,23 @@ __device__ __forceinline__ void dequant_role(const Sched& sched, SegState& ss, u
     }
 }
 
-template <int FMT, bool BF16, int BT>
+// PAIR: launched as clusters of 2 CTAs sharing each 256-weight-row tile (tcgen05 cta_group::2).
+// Each CTA dequantizes its own 128 weight rows and loads half of the activation rows; the leader
+// (cluster rank 0) issues M=256 MMAs that read both CTAs' shared memory and write each CTA's
+// 128-row accumulator; completions are committed to both CTAs. Halving the activation bytes each
+// SM loads per k-block is the point: at BT=256 those tiles, not the MMAs, bound the main loop.
+template <int FMT, bool BF16, int BT, bool PAIR>
 __global__ void __launch_bounds__(THREADS, 1)
 gemm_tc_kernel(const __grid_constant__ CUtensorMap tm_x, const __grid_constant__ CUtensorMap tm_w, WView w,
                float* __restrict__ out, int64_t m, int64_t ldo, Sched sched, float* __restrict__ ws_part,
                uint32_t* __restrict__ ws_flag, uint32_t* err) {
-    using L = Smem<FMT, BT>;
+    using L = Smem<FMT, BT, PAIR>;
     constexpr int SX = L::SX, SA = L::SA;
     constexpr bool QUANT = FMT != FMT_F16;
+    static_assert(!PAIR || QUANT, "pairs are for quantized weights");
+    constexpr int TW = PAIR ? 2 * BW : BW;  // weight rows per tile
     constexpr uint32_t TMEM_COLS = 2 * BT;
-    constexpr uint32_t IDESC = idesc_f16(BF16, BW, BT);
+    constexpr uint32_t IDESC = idesc_f16(BF16, TW, BT);
 
     extern __shared__ uint8_t smem_raw[];
     uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
@@ -529,7 +587,10 @@ gemm_tc_kernel(const __grid_constant__ CUtensorMap tm_x, const __grid_constant__
 
     const int warp = threadIdx.x >> 5;
     const int lane = threadIdx.x & 31;
-    const int cta = blockIdx.x;
+    const int cta = blockIdx.x;                          // partial-tile slot and flag of this CTA
+    const int rank = PAIR ? (int)cluster_ctarank() : 0;  // 128-row half of the pair's weight rows
+    const int unit = PAIR ? cta >> 1 : cta;              // schedule unit (CTA or pair)
+    auto cid = [&](int u) { return PAIR ? 2 * u + rank : u; };  // CTA of unit u holding our half
 
     if (threadIdx.x == 0) {
         for (int s = 0; s < SX; ++s) {
@@ -537,7 +598,8 @@ gemm_tc_kernel(const __grid_constant__ CUtensorMap tm_x, const __grid_constant__
             mbar_init(empty_b(s), 1);
         }
         for (int s = 0; s < SA; ++s) {
-            mbar_init(full_a(s), DQ_WARPS / 2);  // one group of dequantizer warps per k-block
+            // one group of dequantizer warps per k-block (in both CTAs of a pair)
+            mbar_init(full_a(s), (PAIR ? 2 : 1) * DQ_WARPS / 2);
             mbar_init(empty_a(s), 1);
         }
         for (int r = 0; r < R; ++r) {
@@ -546,24 +608,30 @@ gemm_tc_kernel(const __grid_constant__ CUtensorMap tm_x, const __grid_constant__
         }
         for (int b = 0; b < 2; ++b) {
             mbar_init(acc_full(b), 1);
-            mbar_init(acc_empty(b), EPI_WARPS);
+            mbar_init(acc_empty(b), (PAIR ? 2 : 1) * EPI_WARPS);
         }
         for (int i = 0; i < L::FIX_NB; ++i) mbar_init(fix_full(i), 1);
         mbar_fence_init();
     }
     if (warp == MMA_WARP) {
-        tmem_alloc(smem_u32(tmem_holder), TMEM_COLS);
-        tmem_relinquish();
+        if constexpr (PAIR) {
+            tmem_alloc_pair(smem_u32(tmem_holder), TMEM_COLS);  // both CTAs of the pair, same holder offset
+            tmem_relinquish_pair();
+        } else {
+            tmem_alloc(smem_u32(tmem_holder), TMEM_COLS);
+            tmem_relinquish();
+        }
     }
     tc_fence_before();
     __syncthreads();
+    if constexpr (PAIR) cluster_sync();  // both CTAs' barriers exist before any remote arrive or copy
     tc_fence_after();
     const uint32_t tmem = *tmem_holder;
     JK_TRACE_POINT(14, 0);
 
     bool ok = true;
     SegState ss;
-    seg_init(sched, cta, ss);
+    seg_init(sched, unit, ss);
     Seg sg;
 
     // The producer, raw-producer and MMA roles run their loops with the whole warp converged (waits
@@ -578,14 +646,21 @@ gemm_tc_kernel(const __grid_constant__ CUtensorMap tm_x, const __grid_constant__
         }
         int it = 0;
         while (ok && seg_next(sched, ss, sg)) {
-            const int32_t n0 = (int32_t)((sg.tile / sched.tiles_m) * BW);
-            const int32_t m0 = (int32_t)((sg.tile % sched.tiles_m) * BT);
+            const int32_t n0 = (int32_t)((sg.tile / sched.tiles_m) * TW + rank * BW);
+            const int32_t m0 = (int32_t)((sg.tile % sched.tiles_m) * BT + (PAIR ? rank * (BT / 2) : 0));
             for (int kb = sg.kb_lo; kb < sg.kb_hi && ok; ++kb) {
                 const int s = it % SX;
                 if (it >= SX) ok = __all_sync(0xFFFFFFFFu, mbar_wait(empty_b(s), ((it / SX) - 1) & 1, err));
                 if (!ok) break;
                 JK_TRACE_POINT(1, it);
-                if (leader) {
+                if constexpr (PAIR) {
+                    // both halves count on the leader's full barrier; only the leader expects them
+                    if (leader) {
+                        if (rank == 0) mbar_expect_tx(full_b(s), 2 * L::B_STAGE);
+                        tma_load_2d_pair(sbase + L::off_b + s * L::B_STAGE, &tm_x, kb * KB, m0,
+                                         mapa_shared(full_b(s), 0));
+                    }
+                } else if (leader) {
                     if constexpr (FMT == FMT_F16) {
                         mbar_expect_tx(full_b(s), L::B_STAGE + A_STAGE_BYTES);
                         tma_load_2d(sbase + L::off_a + s * A_STAGE_BYTES, &tm_w, kb * KB, n0, full_b(s));
@@ -598,14 +673,16 @@ gemm_tc_kernel(const __grid_constant__ CUtensorMap tm_x, const __grid_constant__
                 ++it;
             }
         }
-        if (!ok)  // drain: every copy this warp issued lands before the CTA may exit
+        // drain: every copy this warp issued lands before the CTA may exit (a pair peer's copies
+        // complete on the leader's barrier; the final cluster barrier covers them)
+        if (!ok && (!PAIR || rank == 0))
             for (int i = it - SX < 0 ? 0 : it - SX; i < it; ++i) mbar_wait(full_b(i % SX), (i / SX) & 1, err);
     } else if (warp == RAW_WARP) {
         // --------------------- raw weight producer: runs up to R super-blocks ahead ---------------------
         if constexpr (QUANT) {
             int raw_n = 0;
             while (ok && seg_next(sched, ss, sg)) {
-                const int32_t n0 = (int32_t)((sg.tile / sched.tiles_m) * BW);
+                const int32_t n0 = (int32_t)((sg.tile / sched.tiles_m) * TW + rank * BW);
                 for (int kb = sg.kb_lo; kb < sg.kb_hi && ok; ++kb) {
                     if (kb != sg.kb_lo && (kb & 3) != 0) continue;
                     const int r = raw_n;
@@ -635,10 +712,14 @@ gemm_tc_kernel(const __grid_constant__ CUtensorMap tm_x, const __grid_constant__
             if (!ok)
                 for (int r = raw_n - R < 0 ? 0 : raw_n - R; r < raw_n; ++r) mbar_wait(raw_full(r % R), (r / R) & 1, err);
         }
-    } else if (warp == MMA_WARP) {
-        // ------------------------------ MMA issuer ------------------------------
+    } else if (warp == MMA_WARP && (!PAIR || rank == 0)) {
+        // ------------------------------ MMA issuer (a pair's leader only) ------------------------------
         int it = 0, seg_i = 0;
         bool issued = false;
+        auto commit = [&](uint32_t bar) {  // arrives once the MMAs issued so far complete
+            if constexpr (PAIR) mma_commit_pair(bar);
+            else mma_commit(bar);
+        };
         while (ok && seg_next(sched, ss, sg)) {
             const int b = seg_i & 1;
             if (seg_i >= 2) ok = __all_sync(0xFFFFFFFFu, mbar_wait(acc_empty(b), ((seg_i >> 1) - 1) & 1, err));
@@ -658,16 +739,20 @@ gemm_tc_kernel(const __grid_constant__ CUtensorMap tm_x, const __grid_constant__
                 const uint64_t bd = sw128_kmajor_desc(sbase + L::off_b + sx * L::B_STAGE);
                 if (leader) {
 #pragma unroll
-                    for (int k = 0; k < KB / 16; ++k)  // +32 bytes per K=16 step inside the swizzle atom
-                        mma_f16(acc, ad + 2u * k, bd + 2u * k, IDESC, (kb > sg.kb_lo || k > 0) ? 1u : 0u);
-                    mma_commit(empty_b(sx));  // each commit arrives once these MMAs complete
-                    if constexpr (QUANT) mma_commit(empty_a(sa));
+                    for (int k = 0; k < KB / 16; ++k) {  // +32 bytes per K=16 step inside the swizzle atom
+                        if constexpr (PAIR)
+                            mma_f16_pair(acc, ad + 2u * k, bd + 2u * k, IDESC, (kb > sg.kb_lo || k > 0) ? 1u : 0u);
+                        else
+                            mma_f16(acc, ad + 2u * k, bd + 2u * k, IDESC, (kb > sg.kb_lo || k > 0) ? 1u : 0u);
+                    }
+                    commit(empty_b(sx));
+                    if constexpr (QUANT) commit(empty_a(sa));
                 }
                 __syncwarp();
                 issued = true;
             }
             if (!ok) break;
-            if (leader) mma_commit(acc_full(b));  // arrives when this segment's MMAs are complete
+            if (leader) commit(acc_full(b));  // arrives when this segment's MMAs are complete
             __syncwarp();
             JK_TRACE_POINT(12, seg_i);
             ++seg_i;
@@ -676,7 +761,7 @@ gemm_tc_kernel(const __grid_constant__ CUtensorMap tm_x, const __grid_constant__
             // Error path: drain the MMAs issued so far before TMEM is released. The commit arrives on
             // acc_full(b) of the unfinished segment; wait for it.
             const int b = seg_i & 1;
-            if (leader) mma_commit(acc_full(b));
+            if (leader) commit(acc_full(b));
             __syncwarp();
             mbar_wait(acc_full(b), (seg_i >> 1) & 1, err);
         }
@@ -696,20 +781,22 @@ gemm_tc_kernel(const __grid_constant__ CUtensorMap tm_x, const __grid_constant__
             tc_fence_after();
             if (!ok) break;
             JK_TRACE_POINT(7, seg_i);
-            const int64_t n0 = (sg.tile / sched.tiles_m) * BW;
+            const int64_t n0 = (sg.tile / sched.tiles_m) * TW + rank * BW;
             const int64_t m0 = (sg.tile % sched.tiles_m) * BT;
             const int64_t wrow = n0 + row_in_tile;
             const bool contributor = sg.kb_lo > 0;
             const bool owner = sg.kb_lo == 0 && sg.kb_hi < sched.kbt;
-            // contributors of an owned tile: the following CTAs whose ranges start inside it
-            int c_last = cta;
+            // contributors of an owned tile: the following units whose ranges start inside it (a
+            // pair CTA combines with the same-rank CTA of each contributing pair)
+            int u_last = unit;
             if (owner) {
                 const int64_t tile_end = (sg.tile + 1) * sched.kbt;
-                while (c_last + 1 < sched.G && sk_start(sched, c_last + 1) < tile_end) ++c_last;
+                while (u_last + 1 < sched.G && sk_start(sched, u_last + 1) < tile_end) ++u_last;
                 __shared__ int flags_ok;
                 if (threadIdx.x == 32 * EPI_WARP0) {
                     bool good = true;
-                    for (int c = cta + 1; c <= c_last && good; ++c) {
+                    for (int u = unit + 1; u <= u_last && good; ++u) {
+                        const int c = cid(u);
                         const uint64_t t0 = globaltimer();
                         while (ld_acquire(ws_flag + c) == 0u) {
                             if (globaltimer() - t0 > WAIT_LIMIT_NS) {
@@ -733,13 +820,13 @@ gemm_tc_kernel(const __grid_constant__ CUtensorMap tm_x, const __grid_constant__
                 // Owner of the CTA's last segment: the contributor partials arrive in shared memory by
                 // bulk copies (round-major, contributor-minor chunks through a FIX_NB ring) instead of
                 // per-thread loads, so a whole ring of them is in flight at once.
-                const int nc = c_last - cta;
+                const int nc = u_last - unit;
                 const bool bulk_fix = owner && nc > 0 && ss.next >= ss.end;
                 const int nchunks = bulk_fix ? (BT / CH) * nc : 0;
                 auto issue_chunk = [&](int q) {
                     const int r = q / nc, ci = q - r * nc;
                     const int g = fix_q + q, buf = g % L::FIX_NB;
-                    const float* src = ws_part + (int64_t)(cta + 1 + ci) * BT * BW + (int64_t)(r * CH) * BW;
+                    const float* src = ws_part + (int64_t)cid(unit + 1 + ci) * BT * BW + (int64_t)(r * CH) * BW;
                     mbar_expect_tx(fix_full(buf), (uint32_t)L::FIX_CHUNK);
                     bulk_g2s(sbase + (uint32_t)(buf * L::FIX_CHUNK), src, (uint32_t)L::FIX_CHUNK, fix_full(buf));
                 };
@@ -787,8 +874,8 @@ gemm_tc_kernel(const __grid_constant__ CUtensorMap tm_x, const __grid_constant__
                                 }
                             }
                         } else {
-                            for (int c = cta + 1; c <= c_last; ++c) {
-                                const float* slot = ws_part + (int64_t)c * BT * BW + (int64_t)c0 * BW + row_in_tile;
+                            for (int u = unit + 1; u <= u_last; ++u) {
+                                const float* slot = ws_part + (int64_t)cid(u) * BT * BW + (int64_t)c0 * BW + row_in_tile;
                                 float p[CH];
 #pragma unroll
                                 for (int j = 0; j < CH; ++j) p[j] = __ldcg(slot + j * BW);
@@ -807,9 +894,10 @@ gemm_tc_kernel(const __grid_constant__ CUtensorMap tm_x, const __grid_constant__
                             for (int j = 0; j < CH; ++j) tp[j * BW + row_in_tile] = acc[j];
                             fence_proxy_async_smem();
                             epi_bar();
-                            if (lane == 0) {
+                            // (a pair CTA's rows can lie wholly past the matrix when rows % 256 != 0)
+                            const int64_t cols = w.rows - n0 < BW ? w.rows - n0 : BW;
+                            if (lane == 0 && cols > 0) {
                                 const int64_t mleft = m - (m0 + c0);
-                                const int64_t cols = w.rows - n0 < BW ? w.rows - n0 : BW;
                                 for (int j = quarter; j < CH && j < mleft; j += EPI_WARPS)
                                     bulk_s2g(out + (m0 + c0 + j) * ldo + n0, smem_u32(tp + j * BW), (uint32_t)(cols * 4));
                                 bulk_commit();
@@ -850,13 +938,16 @@ gemm_tc_kernel(const __grid_constant__ CUtensorMap tm_x, const __grid_constant__
                 } else if (owner) {
                     epi_bar();  // all partial reads done: clear the flags for the next launch
                     if (threadIdx.x == 32 * EPI_WARP0)
-                        for (int c = cta + 1; c <= c_last; ++c) ws_flag[c] = 0u;
+                        for (int u = unit + 1; u <= u_last; ++u) ws_flag[cid(u)] = 0u;
                 }
             }
             tc_fence_before();
             __syncwarp();
             JK_TRACE_POINT(8, seg_i);
-            if (lane == 0) mbar_arrive(acc_empty(b));
+            if (lane == 0) {  // the MMA issuer (a pair's leader) may overwrite this accumulator
+                if constexpr (PAIR) mbar_arrive_cluster(mapa_shared(acc_empty(b), 0));
+                else mbar_arrive(acc_empty(b));
+            }
             ++seg_i;
         }
     } else if (dq_slot(warp) >= 0) {
@@ -864,16 +955,20 @@ gemm_tc_kernel(const __grid_constant__ CUtensorMap tm_x, const __grid_constant__
         if constexpr (QUANT) {
             const int t = 32 * dq_slot(warp) + lane;  // 0..255
             const int row_in_tile = t & (BW - 1);
-            dequant_role<FMT, BF16, BT>(sched, ss, smem, row_in_tile, t / BW, w, err, ok, bar0, lane);
+            dequant_role<FMT, BF16, BT, PAIR>(sched, ss, smem, row_in_tile, t / BW, rank, w, err, ok, bar0, lane);
         }
     }
 
     tc_fence_before();
     __syncthreads();
+    // a pair CTA may still receive the peer's arrives and have its shared memory read by the
+    // leader's MMAs until both are here
+    if constexpr (PAIR) cluster_sync();
     JK_TRACE_POINT(15, 0);
     if (warp == MMA_WARP) {
         tc_fence_after();
-        tmem_dealloc(tmem, TMEM_COLS);
+        if constexpr (PAIR) tmem_dealloc_pair(tmem, TMEM_COLS);
+        else tmem_dealloc(tmem, TMEM_COLS);
     }
 }
 
@@ -894,7 +989,8 @@ int prepare_kernel(K kern, int smem, int device, int (&cache)[64]) {
 
 struct LaunchArgs {
     const jk_qmatrix* wq;
-    const CUtensorMap* tm_x;
+    const CUtensorMap* tm_x;  // box rows BT (BT / 2 for pair launches)
+    bool pair;                // clusters of 2 CTAs (cta_group::2) for quantized weights at BT >= 128
     float* out;
     int64_t m, ldo;
     bool stream_k;
@@ -904,10 +1000,11 @@ struct LaunchArgs {
     cudaStream_t stream;
 };
 
-template <int FMT, bool BF16, int BT>
+template <int FMT, bool BF16, int BT, bool PAIR>
 jk_status launch_tc(const LaunchArgs& a) {
-    using L = Smem<FMT, BT>;
-    auto kern = gemm_tc_kernel<FMT, BF16, BT>;
+    using L = Smem<FMT, BT, PAIR>;
+    auto kern = gemm_tc_kernel<FMT, BF16, BT, PAIR>;
+    constexpr int TW = PAIR ? 2 * BW : BW;
     int dev = 0;
     cudaGetDevice(&dev);
     static int per_sm_cache[64] = {};
@@ -916,26 +1013,69 @@ jk_status launch_tc(const LaunchArgs& a) {
     const WView& w = a.wq->view;
     Sched s;
     s.tiles_m = (int)((a.m + BT - 1) / BT);
-    s.tiles = ((w.rows + BW - 1) / BW) * s.tiles_m;
+    s.tiles = ((w.rows + TW - 1) / TW) * s.tiles_m;
     s.kbt = (int)(w.k / KB);
     s.sk = a.stream_k ? 1 : 0;
-    int64_t g = (int64_t)sm_budget(dev) * per_sm;
-    if (a.grid_cap > 0 && g > a.grid_cap) g = a.grid_cap;
     const int64_t work = s.sk ? s.tiles * s.kbt : s.tiles;
-    if (g > work) g = work;
-    s.G = (int)g;
-    kern<<<s.G, THREADS, L::total, a.stream>>>(*a.tm_x, a.wq->tm_w, w, a.out, a.m, a.ldo, s, a.ws_part, a.ws_flag,
-                                               device_error_word(a.wq->device));
-    return cuda_fail(cudaGetLastError(), "gemm launch");
+    if constexpr (PAIR) {
+        cudaLaunchConfig_t cfg = {};
+        cfg.blockDim = dim3(THREADS);
+        cfg.dynamicSmemBytes = L::total;
+        cfg.stream = a.stream;
+        cudaLaunchAttribute attr[1];
+        attr[0].id = cudaLaunchAttributeClusterDimension;
+        attr[0].val.clusterDim.x = 2;
+        attr[0].val.clusterDim.y = 1;
+        attr[0].val.clusterDim.z = 1;
+        cfg.attrs = attr;
+        cfg.numAttrs = 1;
+        // pairs that can be resident at once (a GPC with an odd SM count leaves one SM unpaired)
+        static int pairs_cache[64] = {};
+        if (dev < 0 || dev >= 64) return fail(JK_ERR_INVALID, "device index out of range");
+        if (!pairs_cache[dev]) {
+            cfg.gridDim = dim3(2 * ((unsigned)sm_count(dev) / 2));
+            int clusters = 0;
+            cudaError_t e = cudaOccupancyMaxActiveClusters(&clusters, kern, &cfg);
+            if (e != cudaSuccess) return cuda_fail(e, "gemm pair occupancy");
+            if (clusters < 1) return fail(JK_ERR_UNSUPPORTED, "gemm: no CTA pair fits on this device");
+            pairs_cache[dev] = clusters;
+        }
+        int64_t g = pairs_cache[dev];
+        const int64_t budget = sm_budget(dev) / 2;
+        if (g > budget) g = budget;
+        if (a.grid_cap > 0 && 2 * g > a.grid_cap) g = a.grid_cap / 2;
+        if (g > work) g = work;
+        if (g < 1) g = 1;
+        s.G = (int)g;
+        cfg.gridDim = dim3(2 * (unsigned)s.G);
+        cudaError_t e = cudaLaunchKernelEx(&cfg, kern, *a.tm_x, a.wq->tm_w, w, a.out, a.m, a.ldo, s, a.ws_part,
+                                           a.ws_flag, device_error_word(a.wq->device));
+        if (e != cudaSuccess) return cuda_fail(e, "gemm pair launch");
+        return cuda_fail(cudaGetLastError(), "gemm pair launch");
+    } else {
+        int64_t g = (int64_t)sm_budget(dev) * per_sm;
+        if (a.grid_cap > 0 && g > a.grid_cap) g = a.grid_cap;
+        if (g > work) g = work;
+        s.G = (int)g;
+        kern<<<s.G, THREADS, L::total, a.stream>>>(*a.tm_x, a.wq->tm_w, w, a.out, a.m, a.ldo, s, a.ws_part,
+                                                   a.ws_flag, device_error_word(a.wq->device));
+        return cuda_fail(cudaGetLastError(), "gemm launch");
+    }
 }
 
 template <int FMT, bool BF16>
 jk_status launch_tc_bt(const LaunchArgs& a, int bt) {
+    if constexpr (FMT != FMT_F16) {
+        if (a.pair) {
+            if (bt == 128) return launch_tc<FMT, BF16, 128, true>(a);
+            if (bt == 256) return launch_tc<FMT, BF16, 256, true>(a);
+        }
+    }
     switch (bt) {
-    case 32: return launch_tc<FMT, BF16, 32>(a);
-    case 64: return launch_tc<FMT, BF16, 64>(a);
-    case 128: return launch_tc<FMT, BF16, 128>(a);
-    default: return launch_tc<FMT, BF16, 256>(a);
+    case 32: return launch_tc<FMT, BF16, 32, false>(a);
+    case 64: return launch_tc<FMT, BF16, 64, false>(a);
+    case 128: return launch_tc<FMT, BF16, 128, false>(a);
+    default: return launch_tc<FMT, BF16, 256, false>(a);
     }
 }
 
@@ -984,18 +1124,21 @@ size_t stream_k_workspace_bytes(int device, int bt) {
     return stream_k_flag_bytes(device) + (size_t)sm_count(device) * 2 * (size_t)bt * BW * 4;
 }
 
-jk_status launch_gemm(const jk_qmatrix* w, const void* x, bool x_bf16, size_t m, float* out, int bt, bool stream_k,
+jk_status launch_gemm(const jk_qmatrix* w, const void* x, bool x_bf16, size_t m, float* out, int bt, bool pair_tile, bool stream_k,
                       void* workspace, size_t workspace_bytes, cudaStream_t stream) {
     if (m == 0) return JK_OK;
     if (!w->has_tmap) return fail(JK_ERR_INVALID, "matrix has no tensor-core layout");
+    // 256-row tiles on CTA pairs (each SM loads half the activation tile); see the plan's bn
+    const bool pair = pair_tile && w->view.fmt != FMT_F16 && bt >= 128;
     CUtensorMap tm_x;
     jk_status st = encode_tmap_2d(&tm_x, x_bf16 ? CU_TENSOR_MAP_DATA_TYPE_BFLOAT16 : CU_TENSOR_MAP_DATA_TYPE_FLOAT16,
-                                  (uint64_t)w->k, (uint64_t)m, (uint64_t)w->k * 2, KB, (uint32_t)bt,
+                                  (uint64_t)w->k, (uint64_t)m, (uint64_t)w->k * 2, KB, (uint32_t)(pair ? bt / 2 : bt),
                                   CU_TENSOR_MAP_SWIZZLE_128B, x);
     if (st != JK_OK) return st;
     LaunchArgs a{};
     a.wq = w;
     a.tm_x = &tm_x;
+    a.pair = pair;
     a.out = out;
     a.m = (int64_t)m;
     a.ldo = w->view.rows;

@@ -61,7 +61,7 @@ jk_status make_weight_tmap(const WView& w, CUtensorMap* map);
 // stream_k_flag_bytes() are zero; otherwise whole tiles per CTA (row invariant).
 size_t stream_k_flag_bytes(int device);
 size_t stream_k_workspace_bytes(int device, int bt);
-jk_status launch_gemm(const jk_qmatrix* w, const void* x, bool x_bf16, size_t m, float* out, int bt,
+jk_status launch_gemm(const jk_qmatrix* w, const void* x, bool x_bf16, size_t m, float* out, int bt, bool pair,
                       bool stream_k, void* workspace, size_t workspace_bytes, cudaStream_t stream);
 jk_status launch_gemm_stream_k_fixed(const jk_qmatrix* w, const void* x, bool x_bf16, size_t m, float* out, int bt,
                                      uint32_t* flags, float* partials, int max_ctas, size_t capacity_bytes,

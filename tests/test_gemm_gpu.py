@@ -18,8 +18,9 @@ def all_plans(w, m):
     from jevons_kernels.gemm import Plan
     plans = [Plan(0, 128, 1)]
     for bm in Plan.ROW_TILES:
-        for splits in (1, 2, 8):
-            plans.append(Plan(bm, 128, splits))
+        for bn in Plan.COL_TILES:
+            for splits in (1, 2, 8):
+                plans.append(Plan(bm, bn, splits))
     return [p for p in plans if p.valid_for(w, m)]
 
 
@@ -123,6 +124,7 @@ def test_plan_validation(gpu):
     assert not Plan(64, 64, 1).valid_for(w, 4)
     assert not Plan(64, 128, 8).valid_for(w, 4)  # k/64 = 4 < 8 splits
     assert not Plan(0, 128, 1).valid_for(w, 17)
+    assert Plan(128, 256, 1).valid_for(w, 4) and not Plan(64, 256, 1).valid_for(w, 4)  # pair tiles: bm >= 128
     x = torch.zeros(4, 256, device="cuda", dtype=torch.bfloat16)
     with pytest.raises(JkError, match="not valid"):
         matmul_plan(gpu, Buf(x), 4, w, Buf(torch.zeros(4, 128, device="cuda")), None, None, Plan(48, 128, 1))
@@ -218,7 +220,8 @@ def test_config4_vocab_head_sampled_and_linear(gpu):
 
 @pytest.mark.parametrize("name,n,k", [("Q4_K", 192, 2560), ("Q8_0", 192, 320), ("Q4_K", 128, 10240), ("Q6_K", 64, 2560)])
 @pytest.mark.parametrize("m", [31, 257])
-def test_stream_k_fixup_shapes(gpu, name, n, k, m):
+@pytest.mark.parametrize("bn", [128, 256])
+def test_stream_k_fixup_shapes(gpu, name, n, k, m, bn):
     """Stream-K fix-up: partial weight tiles (n % 128 != 0), partial row tiles, tiles split over
     many CTAs (k = 10240 on one weight tile), and output rows that are not 16-byte aligned (the
     per-element store path). A spare element after the output must stay untouched."""
@@ -227,14 +230,14 @@ def test_stream_k_fixup_shapes(gpu, name, n, k, m):
     x, x_exact = activations(m, k, torch.bfloat16, seed=m + 1)
     want = oracle.matmul_f64(x_exact, dense)
     scratch = SplitScratch(gpu)
-    for bm in (32, 256):
+    for bm in (32, 256) if bn == 128 else (128, 256):
         for splits in (2, 4):
-            assert Plan(bm, 128, splits).valid_for(w, m)
+            assert Plan(bm, bn, splits).valid_for(w, m)
             for shift in (0, 1):
                 big = torch.full((m * n + 2,), float("nan"), device="cuda")
                 out = big[shift:shift + m * n].view(m, n)
                 matmul_plan(gpu, Buf(x), m, w, Buf(out), None, scratch,
-                            Plan(bm, 128, splits))
+                            Plan(bm, bn, splits))
                 assert_close(f"{name} {n}x{k} m={m} bm={bm} s={splits} shift={shift}", out.cpu().numpy(), x_exact,
                              dense, want)
                 assert torch.isnan(big[shift + m * n]).item()

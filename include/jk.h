@@ -200,6 +200,54 @@ jk_status jk_matmul_tiled(const jk_qmatrix *w, const void *x, int x_dtype, size_
 jk_status jk_f16_linear(const void *x_f16, size_t m, size_t k, const void *w_f16, size_t n,
                         float *out, void *stream);
 
+/* ---- expert-grouped products ----------------------------------------------------------------- */
+
+/* Groups (gemm.rs:955-966): a device-side grouping of routed rows by expert, as written by
+ * jk_group_experts. Job j covers sorted positions [jobs[2j+2], min(jobs[2j+2] + tile,
+ * offsets[e+1])) of expert e = jobs[2j+1] (jobs[0] = job count), where tile is the row tile the
+ * jobs were built with; position s reads activation row sorted[s] / in_div and writes output row
+ * sorted[s] (gemm.rs:9-11). */
+typedef struct jk_groups {
+    const uint32_t *sorted;  /* [rows] assignment index of each sorted position (the reference's ids) */
+    const uint32_t *offsets; /* [experts + 1] first sorted position of each expert, then the total */
+    const uint32_t *jobs;    /* [1 + 2 * max_jobs] job count, then (expert, first position) pairs */
+    size_t max_jobs;         /* upper bound on the job count: the grid's job dimension */
+    uint32_t in_div;         /* activation row = assignment / in_div (top_k for per-token inputs) */
+    size_t rows;             /* output rows (assignments) */
+} jk_groups;
+
+/* The job bound jk_group_experts needs room for: ceil(assignments / bm) + min(experts,
+ * assignments). The reference's callers size jobs as ceil(a / bm) + experts
+ * (crates/jevons-gemma4-diffusion/src/model.rs:593), which is never smaller. 0 if bm < 1. */
+size_t jk_group_max_jobs(size_t assignments, size_t experts, int bm);
+
+/* group_routes (crates/jevons-gemma4-diffusion/src/gpu/ops.rs:1100-1128, kernel `group`
+ * :523-585): deterministic grouping of `assignments` expert ids (device u32, each < experts) on
+ * `stream`. Writes sorted[assignments] (assignment indices ordered by expert, ascending within
+ * an expert), offsets[experts + 1] and jobs (jobs[0] = count, then (expert, start) pairs for tiles
+ * of bm rows, experts ascending). jobs_len (elements) must hold 1 + 2 * jk_group_max_jobs(...).
+ * experts <= 1024. An id >= experts is left out of every group (offsets[experts] then counts
+ * fewer rows and the products never write those rows) and sets an error bit that
+ * jk_device_error reports. */
+jk_status jk_group_experts(int device, const uint32_t *ids, size_t assignments, size_t experts, int bm,
+                           uint32_t *sorted, uint32_t *offsets, uint32_t *jobs, size_t jobs_len, void *stream);
+
+/* matmul_grouped (gemm.rs:1271-1321): out[sorted[s], :] = x[sorted[s] / in_div, :] . W_e^T for
+ * every sorted position s of expert e, W_e = rows [e * n, (e + 1) * n) of the matrix, on the
+ * tensor cores. The jobs must have been built with tiles of bm rows. bm/bn as in jk_plan; splits
+ * (1..16, k / 64 >= splits) is accepted for plan compatibility, and every split count gives the
+ * whole-K result of splits = 1 (jobs are read on the device, so the product always runs whole
+ * tiles and stays row invariant). x: x_len / k activation rows (f32, f16 or bf16); the activation
+ * rows are gathered into `scratch` (required) in sorted order first. out_len >= rows * n. */
+jk_status jk_matmul_grouped(const jk_qmatrix *w, const void *x, int x_dtype, size_t x_len, const jk_groups *g,
+                            float *out, size_t out_len, int bm, int bn, int splits, jk_split_scratch *scratch,
+                            void *stream);
+
+/* matvec_grouped (gemm.rs:1170-1200): the grouped product on the small-row kernel, for jobs built
+ * with tiles of mr <= JK_GEMV_ROWS rows. Reads activation rows in place (no scratch). */
+jk_status jk_matvec_grouped(const jk_qmatrix *w, const void *x, int x_dtype, size_t x_len, const jk_groups *g,
+                            float *out, size_t out_len, int mr, void *stream);
+
 /* ---- allocation-free product ----------------------------------------------------------------- */
 
 /* Size of the device buffer libjk.so declares for jk_matmul_splitk_noalloc (per GPU, held from

@@ -816,6 +816,113 @@ extern "C" jk_status jk_matmul_plan(const jk_qmatrix* w, const void* x, int x_dt
     return jk::launch_gemm(&dense, xk, want_bf16, m, out, plan.bm, plan.bn == 256, stream_k, sbuf, ws_bytes, cs);
 }
 
+// ================================================================================================
+// expert-grouped products
+// ================================================================================================
+extern "C" size_t jk_group_max_jobs(size_t assignments, size_t experts, int bm) {
+    if (bm < 1) return 0;
+    return (assignments + (size_t)bm - 1) / (size_t)bm + (experts < assignments ? experts : assignments);
+}
+
+extern "C" jk_status jk_group_experts(int device, const uint32_t* ids, size_t assignments, size_t experts, int bm,
+                                      uint32_t* sorted, uint32_t* offsets, uint32_t* jobs, size_t jobs_len,
+                                      void* stream) {
+    if (experts == 0 || experts > jk::GROUP_MAX_EXPERTS)
+        return fail(JK_ERR_UNSUPPORTED, "grouping takes 1..1024 experts");
+    if (bm < 1) return fail(JK_ERR_INVALID, "grouping row tile must be positive");
+    if (assignments > (size_t)INT32_MAX) return fail(JK_ERR_INVALID, "too many assignments");
+    if (!offsets || !jobs || (assignments && (!ids || !sorted))) return fail(JK_ERR_INVALID, "null grouping buffer");
+    const size_t need = jk_group_max_jobs(assignments, experts, bm);
+    if (jobs_len < 1 + 2 * need) {
+        char buf[160];
+        snprintf(buf, sizeof buf, "jobs buffer holds %zu words; %zu routes over %zu experts at bm=%d need %zu", jobs_len,
+                 assignments, experts, bm, 1 + 2 * need);
+        return fail(JK_ERR_INVALID, buf);
+    }
+    DeviceGuard g(device);
+    return jk::launch_group_experts(ids, assignments, experts, bm, (jobs_len - 1) / 2 < (size_t)UINT32_MAX
+                                        ? (jobs_len - 1) / 2 : (size_t)UINT32_MAX,
+                                    sorted, offsets, jobs, jk::device_error_word(device),
+                                    static_cast<cudaStream_t>(stream));
+}
+
+namespace {
+
+// Shared checks of the grouped products; sets *x_rows to the activation rows x holds.
+jk_status check_grouped(const jk_qmatrix* w, const void* x, int x_dtype, size_t x_len, const jk_groups* g,
+                        const float* out, size_t out_len, size_t* x_rows) {
+    if (!w || !g) return fail(JK_ERR_INVALID, "null matrix or groups");
+    if (x_dtype != JK_DTYPE_F32 && x_dtype != JK_DTYPE_F16 && x_dtype != JK_DTYPE_BF16)
+        return fail(JK_ERR_INVALID, "unknown activation dtype");
+    if (g->in_div < 1) return fail(JK_ERR_INVALID, "groups: in_div must be >= 1");
+    const size_t need_x = (g->rows + g->in_div - 1) / g->in_div;
+    if (out_len < g->rows * w->n || x_len < need_x * w->k) {
+        char buf[220];
+        snprintf(buf, sizeof buf, "%s: buffers too small for %zu grouped rows (x %zu < %zu or out %zu < %zu)",
+                 shape_str(w->type, w->experts, w->n, w->k).c_str(), g->rows, x_len, need_x * w->k, out_len,
+                 g->rows * w->n);
+        return fail(JK_ERR_INVALID, buf);
+    }
+    if (g->rows && (!x || !out || !g->sorted || !g->offsets || !g->jobs))
+        return fail(JK_ERR_INVALID, "null activation, output or grouping pointer");
+    if (g->rows > (size_t)INT32_MAX || g->max_jobs > (size_t)INT32_MAX) return fail(JK_ERR_INVALID, "groups too large");
+    *x_rows = x_len / w->k;
+    return JK_OK;
+}
+
+}  // namespace
+
+extern "C" jk_status jk_matmul_grouped(const jk_qmatrix* w, const void* x, int x_dtype, size_t x_len,
+                                       const jk_groups* g, float* out, size_t out_len, int bm, int bn, int splits,
+                                       jk_split_scratch* scratch, void* stream) {
+    size_t x_rows = 0;
+    jk_status st = check_grouped(w, x, x_dtype, x_len, g, out, out_len, &x_rows);
+    if (st != JK_OK) return st;
+    const jk_plan plan{bm, bn, splits};
+    if (bm == 0 || !plan_valid(plan, w, 1)) {
+        char buf[160];
+        snprintf(buf, sizeof buf, "grouped plan {bm %d, bn %d, splits %d} is not valid for %s", bm, bn, splits,
+                 shape_str(w->type, w->experts, w->n, w->k).c_str());
+        return fail(JK_ERR_INVALID, buf);
+    }
+    if (g->rows == 0 || g->max_jobs == 0) return JK_OK;
+    const bool f16_weights = w->type == JK_TYPE_F16;
+    if (f16_weights && x_dtype != JK_DTYPE_F16) return fail(JK_ERR_UNSUPPORTED, "FP16 weights need FP16 activations");
+    if (!scratch) return fail(JK_ERR_INVALID, "grouped products need a scratch for the sorted activation rows");
+    if (scratch->device != w->device) return fail(JK_ERR_INVALID, "scratch belongs to another device");
+    DeviceGuard dg(w->device);
+    cudaStream_t cs = static_cast<cudaStream_t>(stream);
+    // operand type: f16 activations stay f16, bf16 and f32 go to bf16 (as in jk_matmul_plan)
+    const bool want_bf16 = x_dtype != JK_DTYPE_F16;
+    // the sorted rows go after the stream-K flag words, which other products on this scratch
+    // expect to find zero
+    const size_t flags = jk::stream_k_flag_bytes(w->device);
+    void* sbuf = nullptr;
+    st = scratch_get(scratch, flags + (g->rows * w->k * 2 + 255) / 256 * 256, &sbuf);
+    if (st != JK_OK) return st;
+    void* xs = static_cast<char*>(sbuf) + flags;
+    st = jk::launch_gather_rows(x, x_dtype, x_rows, w->k, g->sorted, g->rows, g->in_div, xs, want_bf16, cs);
+    if (st != JK_OK) return st;
+    return jk::launch_gemm_grouped(w, xs, want_bf16, g->rows, g->sorted, g->offsets, g->jobs, g->max_jobs, bm, out,
+                                   bm, bn == 256, cs);
+}
+
+extern "C" jk_status jk_matvec_grouped(const jk_qmatrix* w, const void* x, int x_dtype, size_t x_len,
+                                       const jk_groups* g, float* out, size_t out_len, int mr, void* stream) {
+    size_t x_rows = 0;
+    jk_status st = check_grouped(w, x, x_dtype, x_len, g, out, out_len, &x_rows);
+    if (st != JK_OK) return st;
+    if (mr < 1 || mr > JK_GEMV_ROWS) {
+        char buf[96];
+        snprintf(buf, sizeof buf, "matvec_grouped takes job tiles of 1..%d rows (got %d)", JK_GEMV_ROWS, mr);
+        return fail(JK_ERR_INVALID, buf);
+    }
+    if (g->rows == 0 || g->max_jobs == 0) return JK_OK;
+    DeviceGuard dg(w->device);
+    return jk::launch_gemv_grouped(w->view, x, x_dtype, x_rows, g->sorted, g->offsets, g->jobs, g->max_jobs,
+                                   g->in_div, mr, g->rows, out, static_cast<cudaStream_t>(stream));
+}
+
 extern "C" jk_status jk_matmul(const jk_qmatrix* w, const void* x, int x_dtype, size_t x_len, size_t m, float* out,
                                size_t out_len, jk_split_scratch* scratch, void* stream) {
     jk_plan p;

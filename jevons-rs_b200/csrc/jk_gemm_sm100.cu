@@ -130,11 +130,46 @@ struct Smem {
 // ------------------------------------------------------------------------------------------------
 struct Sched {
     int64_t tiles;     // weight tiles * activation tiles
-    int tiles_m;       // activation-row tiles
+    int tiles_m;       // activation-row tiles (grouped: jobs, an upper bound)
     int kbt;           // k-blocks per tile
     int G;             // CTAs
     int sk;            // 1 = stream-K, 0 = whole tiles
+    // Expert-grouped products (whole tiles only): activation rows are expert-sorted; job j covers
+    // sorted rows [jobs[2j+2], min(jobs[2j+2] + BT, offsets[e+1])) of expert e = jobs[2j+1]
+    // (jobs[0] = job count, read on the device) and writes output rows sorted[s].
+    const uint32_t* jobs;     // null: dense product
+    const uint32_t* offsets;
+    const uint32_t* sorted;
+    int64_t n_exp;            // weight rows (output columns) per expert
+    int job_rows;             // rows per job (<= BT)
 };
+
+// Where a tile sits: its first weight row in the matrix, the first output column, its
+// activation rows [m0, mend) and (grouped) whether its job exists.
+struct TileAt {
+    int64_t wrow0, col0, m0, mend;
+    bool live;
+};
+template <int TW, int BT>
+__device__ __forceinline__ TileAt tile_at(const Sched& s, int64_t tile, int rank, int64_t m) {
+    TileAt t;
+    const int64_t wt = tile / s.tiles_m, mt = tile % s.tiles_m;
+    t.col0 = wt * TW + rank * 128;
+    if (!s.jobs) {
+        t.wrow0 = t.col0;
+        t.m0 = mt * BT;
+        t.mend = m;
+        t.live = true;
+    } else {
+        t.live = mt < (int64_t)__ldg(s.jobs);
+        const int64_t e = t.live ? __ldg(s.jobs + 1 + 2 * mt) : 0;
+        t.m0 = t.live ? __ldg(s.jobs + 2 + 2 * mt) : 0;
+        const int64_t end = t.live ? __ldg(s.offsets + e + 1) : 0;
+        t.mend = end < t.m0 + s.job_rows ? end : t.m0 + s.job_rows;
+        t.wrow0 = e * s.n_exp + t.col0;
+    }
+    return t;
+}
 
 struct Seg {
     int64_t tile;
@@ -230,6 +265,11 @@ __device__ __forceinline__ bool seg_next(const Sched& s, SegState& st, Seg& g) {
         g.kb_hi = left < (int64_t)(s.kbt - g.kb_lo) ? g.kb_lo + (int)left : s.kbt;
         st.next += g.kb_hi - g.kb_lo;
     } else {
+        if (s.jobs) {  // grouped: every role skips the tiles of jobs past the device-side count
+            const int64_t njobs = (int64_t)__ldg(s.jobs);
+            while (st.next < st.end && st.next % s.tiles_m >= njobs) st.next += s.G;
+            if (st.next >= st.end) return false;
+        }
         g.tile = st.next;
         g.kb_lo = 0;
         g.kb_hi = s.kbt;
@@ -503,7 +543,7 @@ __device__ __forceinline__ void dequant_role(const Sched& sched, SegState& ss, u
     int it = 0, raw_n = 0;
     Seg sg;
     while (ok && seg_next(sched, ss, sg)) {
-        const int64_t row = (sg.tile / sched.tiles_m) * TW + rank * BW + row_in_tile;
+        const int64_t row = tile_at<TW, BT>(sched, sg.tile, rank, 0).wrow0 + row_in_tile;
         const bool row_ok = row < w.rows;
         const int64_t rr = row_ok ? row : 0;
         const int sb_lo = sg.kb_lo >> 2, sb_hi = (sg.kb_hi - 1) >> 2;
@@ -646,8 +686,9 @@ gemm_tc_kernel(const __grid_constant__ CUtensorMap tm_x, const __grid_constant__
         }
         int it = 0;
         while (ok && seg_next(sched, ss, sg)) {
-            const int32_t n0 = (int32_t)((sg.tile / sched.tiles_m) * TW + rank * BW);
-            const int32_t m0 = (int32_t)((sg.tile % sched.tiles_m) * BT + (PAIR ? rank * (BT / 2) : 0));
+            const TileAt ta = tile_at<TW, BT>(sched, sg.tile, rank, m);
+            const int32_t n0 = (int32_t)ta.wrow0;
+            const int32_t m0 = (int32_t)(ta.m0 + (PAIR ? rank * (BT / 2) : 0));
             for (int kb = sg.kb_lo; kb < sg.kb_hi && ok; ++kb) {
                 const int s = it % SX;
                 if (it >= SX) ok = __all_sync(0xFFFFFFFFu, mbar_wait(empty_b(s), ((it / SX) - 1) & 1, err));
@@ -682,7 +723,7 @@ gemm_tc_kernel(const __grid_constant__ CUtensorMap tm_x, const __grid_constant__
         if constexpr (QUANT) {
             int raw_n = 0;
             while (ok && seg_next(sched, ss, sg)) {
-                const int32_t n0 = (int32_t)((sg.tile / sched.tiles_m) * TW + rank * BW);
+                const int32_t n0 = (int32_t)tile_at<TW, BT>(sched, sg.tile, rank, m).wrow0;
                 for (int kb = sg.kb_lo; kb < sg.kb_hi && ok; ++kb) {
                     if (kb != sg.kb_lo && (kb & 3) != 0) continue;
                     const int r = raw_n;
@@ -781,8 +822,9 @@ gemm_tc_kernel(const __grid_constant__ CUtensorMap tm_x, const __grid_constant__
             tc_fence_after();
             if (!ok) break;
             JK_TRACE_POINT(7, seg_i);
-            const int64_t n0 = (sg.tile / sched.tiles_m) * TW + rank * BW;
-            const int64_t m0 = (sg.tile % sched.tiles_m) * BT;
+            const TileAt ta = tile_at<TW, BT>(sched, sg.tile, rank, m);
+            const int64_t n0 = ta.col0;  // output column of TMEM lane 0 (dense: also its weight row)
+            const int64_t m0 = ta.m0;
             const int64_t wrow = n0 + row_in_tile;
             const bool contributor = sg.kb_lo > 0;
             const bool owner = sg.kb_lo == 0 && sg.kb_hi < sched.kbt;
@@ -902,12 +944,21 @@ gemm_tc_kernel(const __grid_constant__ CUtensorMap tm_x, const __grid_constant__
                                     bulk_s2g(out + (m0 + c0 + j) * ldo + n0, smem_u32(tp + j * BW), (uint32_t)(cols * 4));
                                 bulk_commit();
                             }
-                        } else if (wrow < w.rows) {
-                            float* o = out + (m0 + c0) * ldo + wrow;
-                            const int64_t mleft = m - (m0 + c0);
+                        } else if (!sched.jobs) {
+                            if (wrow < w.rows) {
+                                float* o = out + (m0 + c0) * ldo + wrow;
+                                const int64_t mleft = m - (m0 + c0);
+#pragma unroll
+                                for (int j = 0; j < CH; ++j)
+                                    if (j < mleft) o[j * ldo] = acc[j];
+                            }
+                        } else if (wrow < sched.n_exp) {
+                            // grouped: sorted row s goes to output row sorted[s] (its assignment)
+                            const int64_t mleft = ta.mend - (m0 + c0);
+                            const uint32_t* srow = sched.sorted + m0 + c0;
 #pragma unroll
                             for (int j = 0; j < CH; ++j)
-                                if (j < mleft) o[j * ldo] = acc[j];
+                                if (j < mleft) out[(int64_t)__ldg(srow + j) * ldo + wrow] = acc[j];
                         }
                     }
                 }
@@ -998,6 +1049,12 @@ struct LaunchArgs {
     uint32_t* ws_flag;
     int grid_cap;  // 0 = SM count x occupancy
     cudaStream_t stream;
+    // expert-grouped product (whole tiles): m = sorted activation rows, ldo = n_exp
+    const uint32_t* jobs = nullptr;
+    const uint32_t* offsets = nullptr;
+    const uint32_t* sorted = nullptr;
+    int64_t n_exp = 0, max_jobs = 0;
+    int job_rows = 0;
 };
 
 template <int FMT, bool BF16, int BT, bool PAIR>
@@ -1011,9 +1068,19 @@ jk_status launch_tc(const LaunchArgs& a) {
     const int per_sm = prepare_kernel(kern, L::total, dev, per_sm_cache);
     if (per_sm < 0) return cuda_fail(cudaGetLastError(), "gemm kernel attributes");
     const WView& w = a.wq->view;
-    Sched s;
-    s.tiles_m = (int)((a.m + BT - 1) / BT);
-    s.tiles = ((w.rows + TW - 1) / TW) * s.tiles_m;
+    Sched s{};
+    if (a.jobs) {
+        s.tiles_m = (int)a.max_jobs;
+        s.tiles = ((a.n_exp + TW - 1) / TW) * s.tiles_m;
+        s.jobs = a.jobs;
+        s.offsets = a.offsets;
+        s.sorted = a.sorted;
+        s.n_exp = a.n_exp;
+        s.job_rows = a.job_rows;
+    } else {
+        s.tiles_m = (int)((a.m + BT - 1) / BT);
+        s.tiles = ((w.rows + TW - 1) / TW) * s.tiles_m;
+    }
     s.kbt = (int)(w.k / KB);
     s.sk = a.stream_k ? 1 : 0;
     const int64_t work = s.sk ? s.tiles * s.kbt : s.tiles;
@@ -1153,6 +1220,35 @@ jk_status launch_gemm(const jk_qmatrix* w, const void* x, bool x_bf16, size_t m,
         a.ws_part = reinterpret_cast<float*>(static_cast<char*>(workspace) + stream_k_flag_bytes(dev));
         a.grid_cap = sm_count(dev) * 2;
     }
+    return x_bf16 ? launch_tc_fmt<true>(a, bt) : launch_tc_fmt<false>(a, bt);
+}
+
+jk_status launch_gemm_grouped(const jk_qmatrix* w, const void* x_sorted, bool x_bf16, size_t rows,
+                              const uint32_t* sorted, const uint32_t* offsets, const uint32_t* jobs, size_t max_jobs,
+                              int job_rows, float* out, int bt, bool pair_tile, cudaStream_t stream) {
+    if (rows == 0 || max_jobs == 0) return JK_OK;
+    if (!w->has_tmap) return fail(JK_ERR_INVALID, "matrix has no tensor-core layout");
+    if (job_rows < 1 || job_rows > bt) return fail(JK_ERR_INVALID, "grouped product: job rows exceed the row tile");
+    const bool pair = pair_tile && w->view.fmt != FMT_F16 && bt >= 128;
+    CUtensorMap tm_x;
+    jk_status st = encode_tmap_2d(&tm_x, x_bf16 ? CU_TENSOR_MAP_DATA_TYPE_BFLOAT16 : CU_TENSOR_MAP_DATA_TYPE_FLOAT16,
+                                  (uint64_t)w->k, (uint64_t)rows, (uint64_t)w->k * 2, KB,
+                                  (uint32_t)(pair ? bt / 2 : bt), CU_TENSOR_MAP_SWIZZLE_128B, x_sorted);
+    if (st != JK_OK) return st;
+    LaunchArgs a{};
+    a.wq = w;
+    a.tm_x = &tm_x;
+    a.pair = pair;
+    a.out = out;
+    a.m = (int64_t)rows;
+    a.ldo = (int64_t)w->n;
+    a.stream = stream;
+    a.jobs = jobs;
+    a.offsets = offsets;
+    a.sorted = sorted;
+    a.n_exp = (int64_t)w->n;
+    a.max_jobs = (int64_t)max_jobs;
+    a.job_rows = job_rows;
     return x_bf16 ? launch_tc_fmt<true>(a, bt) : launch_tc_fmt<false>(a, bt);
 }
 

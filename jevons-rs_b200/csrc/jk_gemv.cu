@@ -72,6 +72,18 @@ struct Geo {
     int x_vec;                  // activations 16-byte aligned: vector loads
 };
 
+// Expert-grouped launch (matvec_grouped): blockIdx.y is the job; job j multiplies sorted rows
+// [jobs[2j+2], min(+job_rows, offsets[e+1])) of expert e = jobs[2j+1] -- activation row
+// sorted[s] / in_div -- by weight rows e*n.., and writes output row sorted[s]. jobs == null: dense.
+struct Grp {
+    const uint32_t* jobs;
+    const uint32_t* offsets;
+    const uint32_t* sorted;
+    uint32_t in_div;
+    int job_rows;
+    int64_t x_rows;   // activation rows (sources past it read as zeros)
+};
+
 __device__ __forceinline__ void bulk_g2s(uint32_t dst, const void* src, uint32_t bytes, uint32_t bar) {
     asm volatile("cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];"
                  :: "r"(dst), "l"(src), "r"(bytes), "r"(bar) : "memory");
@@ -152,7 +164,8 @@ __device__ __forceinline__ void load8(const void* x, int x_dtype, int64_t idx, b
 // Stage x rows [0, MR) (rows >= mrows as zeros) into the int16 slot layout. Each thread takes
 // 8-element chunks; the 4 chunks of a 32-element block sit in 4 consecutive lanes.
 template <int FMT, int MR>
-__device__ __forceinline__ void stage_x(const Geo& geo, const void* x, int x_dtype, int mrows, uint32_t* xs) {
+__device__ __forceinline__ void stage_x(const Geo& geo, const void* x, int x_dtype, int mrows, uint32_t* xs,
+                                        const int64_t (&src)[MR]) {
     constexpr int U = 4;
     const int kc = geo.k / 8;                 // chunks per row
     const int chunks = (int)MR * kc;
@@ -163,8 +176,8 @@ __device__ __forceinline__ void stage_x(const Geo& geo, const void* x, int x_dty
         for (int u = 0; u < U; ++u) {
             const int c = c0 + u * THREADS + threadIdx.x;
             const int r = MR == 1 ? 0 : c / kc;
-            if (c < chunks && r < mrows) {
-                load8(x, x_dtype, (int64_t)r * geo.k + (c - r * kc) * 8, geo.x_vec != 0, v[u]);
+            if (c < chunks && r < mrows && src[r] >= 0) {
+                load8(x, x_dtype, src[r] * geo.k + (c - r * kc) * 8, geo.x_vec != 0, v[u]);
             } else {
 #pragma unroll
                 for (int i = 0; i < 8; ++i) v[u][i] = 0.f;
@@ -210,7 +223,7 @@ __device__ __forceinline__ void stage_x(const Geo& geo, const void* x, int x_dty
 template <int FMT, int MR>
 __global__ void __launch_bounds__(THREADS, MR <= 2 ? 2 : 1) gemv_kernel(WView w, Geo geo, const void* __restrict__ x, int x_dtype,
                                                           int mrows, float* __restrict__ out, int64_t ldo,
-                                                          uint32_t* err) {
+                                                          uint32_t* err, Grp gp) {
     extern __shared__ __align__(128) uint8_t smem[];
     __shared__ __align__(8) uint64_t bars[WARPS * SLOTS_PER_WARP];
     uint32_t* xs = reinterpret_cast<uint32_t*>(smem);
@@ -219,6 +232,29 @@ __global__ void __launch_bounds__(THREADS, MR <= 2 ? 2 : 1) gemv_kernel(WView w,
 
     pdl_trigger();  // the next product may start its weight stream as soon as it fits on an SM
     JK_TRACE_POINT(1, 0);
+
+    // activation row of each staged row, output row offset of each, first weight row
+    int64_t src[MR], dst[MR];
+    int64_t wrow0 = 0;
+#pragma unroll
+    for (int r = 0; r < MR; ++r) src[r] = dst[r] = r;
+    if (gp.jobs) {
+        // the job table comes from the previous grid (the grouping): wait for it first
+        pdl_wait();
+        const uint32_t j = blockIdx.y;
+        if (j >= __ldg(gp.jobs)) return;  // CTA-uniform: past the job count
+        const uint32_t e = __ldg(gp.jobs + 1 + 2 * j), s0 = __ldg(gp.jobs + 2 + 2 * j);
+        const uint32_t end = __ldg(gp.offsets + e + 1);
+        mrows = (int)(end < s0 + (uint32_t)gp.job_rows ? end - s0 : (uint32_t)gp.job_rows);
+        if (mrows > MR) mrows = MR;
+        wrow0 = (int64_t)e * w.n;
+#pragma unroll
+        for (int r = 0; r < MR; ++r) {
+            const int64_t a = r < mrows ? (int64_t)__ldg(gp.sorted + s0 + r) : -1;
+            src[r] = a >= 0 && a / gp.in_div < gp.x_rows ? a / gp.in_div : -1;
+            dst[r] = a;
+        }
+    }
 
     const int lane = threadIdx.x & 31;
     const int warp = threadIdx.x >> 5;
@@ -257,17 +293,17 @@ __global__ void __launch_bounds__(THREADS, MR <= 2 ? 2 : 1) gemv_kernel(WView w,
         uint32_t bytes = 0, qb = 0, db = 0, hb = 0;
         const uint8_t *qs = nullptr, *ds = nullptr, *hs = nullptr;
         if (lane < GROUP_ROWS) {
-            const int row = rg * GROUP_ROWS + lane;
-            qs = w.q + (int64_t)row * w.q_row_bytes + (int64_t)e0 * geo.qsb / 256;
+            const int64_t row = wrow0 + rg * GROUP_ROWS + lane;
+            qs = w.q + row * w.q_row_bytes + (int64_t)e0 * geo.qsb / 256;
             qb = (uint32_t)((e1 - e0) * geo.qsb / 256);
             if (geo.dsb) {
-                const uintptr_t a = reinterpret_cast<uintptr_t>(w.d) + (int64_t)row * geo.d_row_bytes + (int64_t)e0 * geo.dsb / 256;
+                const uintptr_t a = reinterpret_cast<uintptr_t>(w.d) + row * geo.d_row_bytes + (int64_t)e0 * geo.dsb / 256;
                 const uintptr_t b = a + (e1 - e0) * geo.dsb / 256;
                 ds = reinterpret_cast<const uint8_t*>(a & ~(uintptr_t)15);
                 db = (uint32_t)(((b + 15) & ~(uintptr_t)15) - (a & ~(uintptr_t)15));
             }
             if (geo.hsb) {
-                const uintptr_t a = reinterpret_cast<uintptr_t>(w.h) + (int64_t)row * geo.h_row_bytes + (int64_t)e0 * geo.hsb / 256;
+                const uintptr_t a = reinterpret_cast<uintptr_t>(w.h) + row * geo.h_row_bytes + (int64_t)e0 * geo.hsb / 256;
                 const uintptr_t b = a + (e1 - e0) * geo.hsb / 256;
                 hs = reinterpret_cast<const uint8_t*>(a & ~(uintptr_t)15);
                 hb = (uint32_t)(((b + 15) & ~(uintptr_t)15) - (a & ~(uintptr_t)15));
@@ -291,7 +327,7 @@ __global__ void __launch_bounds__(THREADS, MR <= 2 ? 2 : 1) gemv_kernel(WView w,
 
     pdl_wait();  // activations come from the previous grid; outputs may be read by it
     JK_TRACE_POINT(3, 0);
-    stage_x<FMT, MR>(geo, x, x_dtype, mrows, xs);
+    stage_x<FMT, MR>(geo, x, x_dtype, mrows, xs, src);
     __syncthreads();
     JK_TRACE_POINT(4, 0);
 
@@ -316,16 +352,16 @@ __global__ void __launch_bounds__(THREADS, MR <= 2 ? 2 : 1) gemv_kernel(WView w,
             const uint8_t* qrow = slot + rsub * geo.q_area;
             const int st0 = st_lo + (int)s * geo.KS;
             const int st1 = st0 + geo.KS < st_hi ? st0 + geo.KS : st_hi;
-            const int row = (first + kk * stride) * GROUP_ROWS + rsub;
+            const int64_t row = wrow0 + (first + kk * stride) * GROUP_ROWS + rsub;
             // start of this row's d / h words inside the slot (the copy began 16-byte aligned)
             const uint8_t* drow = nullptr;
             const uint8_t* hrow = nullptr;
             if (geo.dsb) {
-                const uintptr_t a = reinterpret_cast<uintptr_t>(w.d) + (int64_t)row * geo.d_row_bytes + st0 * geo.dsb;
+                const uintptr_t a = reinterpret_cast<uintptr_t>(w.d) + row * geo.d_row_bytes + st0 * geo.dsb;
                 drow = slot + GROUP_ROWS * geo.q_area + rsub * geo.d_area + (a & 15);
             }
             if (geo.hsb) {
-                const uintptr_t a = reinterpret_cast<uintptr_t>(w.h) + (int64_t)row * geo.h_row_bytes + st0 * geo.hsb;
+                const uintptr_t a = reinterpret_cast<uintptr_t>(w.h) + row * geo.h_row_bytes + st0 * geo.hsb;
                 hrow = slot + GROUP_ROWS * (geo.q_area + geo.d_area) + rsub * geo.h_area + (a & 15);
             }
 #pragma unroll 2
@@ -506,7 +542,7 @@ __global__ void __launch_bounds__(THREADS, MR <= 2 ? 2 : 1) gemv_kernel(WView w,
             if (live && ok && g == 0) {
 #pragma unroll
                 for (int r = 0; r < MR; ++r)
-                    if (r < mrows) out[(int64_t)r * ldo + row] = acc[r];
+                    if (r < mrows) out[dst[r] * ldo + row] = acc[r];
             }
         } else {
             float* rb = red + (size_t)(kk & 1) * WARPS * MR * GROUP_ROWS;
@@ -520,7 +556,7 @@ __global__ void __launch_bounds__(THREADS, MR <= 2 ? 2 : 1) gemv_kernel(WView w,
                 for (int r = 0; r < MR; ++r) {
                     float v = 0.f;
                     for (int q = 0; q < P; ++q) v += rb[((warp + q) * MR + r) * GROUP_ROWS + rsub];
-                    if (r < mrows) out[(int64_t)r * ldo + row] = v;
+                    if (r < mrows) out[dst[r] * ldo + row] = v;
                 }
             }
         }
@@ -537,9 +573,10 @@ struct Cache {
     int smem_set[64];
 };
 
+// gp.jobs != null: grouped launch over `jobs_y` jobs (grid y), about `jobs_est` of them live.
 template <int FMT, int MR>
 jk_status launch_gemv_t(const WView& w, const void* x, int x_dtype, int mrows, float* out, int64_t ldo,
-                        cudaStream_t stream) {
+                        cudaStream_t stream, const Grp& gp = Grp{}, unsigned jobs_y = 1, int64_t jobs_est = 1) {
     int dev = 0;
     cudaGetDevice(&dev);
     const int sms = sm_budget(dev);
@@ -548,7 +585,7 @@ jk_status launch_gemv_t(const WView& w, const void* x, int x_dtype, int mrows, f
         return fail(JK_ERR_UNSUPPORTED, "gemv: matrix too large for 32-bit indexing");
     geo.k = (int)w.k;
     geo.steps = (int)((w.k + 255) / 256);
-    geo.rowgroups = (int)(w.rows / GROUP_ROWS);
+    geo.rowgroups = (int)((gp.jobs ? w.n : w.rows) / GROUP_ROWS);
     switch (FMT) {
     case FMT_Q4K: geo.qsb = 144; break;
     case FMT_Q6K: geo.qsb = 208; geo.dsb = 2; break;
@@ -566,7 +603,8 @@ jk_status launch_gemv_t(const WView& w, const void* x, int x_dtype, int mrows, f
 
     // warps per row group: enough warp items for 8 warps per SM, never more parts than steps
     geo.P = 1;
-    while (geo.P < WARPS && (int64_t)geo.rowgroups * geo.P < (int64_t)sms * WARPS * WARP_TARGET && 2 * geo.P <= geo.steps)
+    while (geo.P < WARPS && (int64_t)geo.rowgroups * jobs_est * geo.P < (int64_t)sms * WARPS * WARP_TARGET &&
+           2 * geo.P <= geo.steps)
         geo.P *= 2;
     const int64_t steps_w = (geo.steps + geo.P - 1) / geo.P;
 
@@ -607,13 +645,14 @@ jk_status launch_gemv_t(const WView& w, const void* x, int x_dtype, int mrows, f
     cudaError_t e = cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, kern, THREADS, smem);
     if (e != cudaSuccess) return cuda_fail(e, "gemv occupancy");
     if (per_sm < 1) return fail(JK_ERR_UNSUPPORTED, "gemv: kernel does not fit on an SM");
-    const int64_t want = (geo.rowgroups * geo.P + WARPS - 1) / WARPS;
-    const int64_t cap = (int64_t)per_sm * sms;
+    const int64_t want = ((int64_t)geo.rowgroups * geo.P + WARPS - 1) / WARPS;
+    // grouped: the live jobs share the SMs
+    const int64_t cap = ((int64_t)per_sm * sms + jobs_est - 1) / jobs_est;
     const unsigned grid = (unsigned)(want < cap ? want : cap);
     if (grid == 0) return JK_OK;
 
     cudaLaunchConfig_t cfg = {};
-    cfg.gridDim = dim3(grid);
+    cfg.gridDim = dim3(grid, jobs_y);
     cfg.blockDim = dim3(THREADS);
     cfg.dynamicSmemBytes = smem;
     cfg.stream = stream;
@@ -622,7 +661,7 @@ jk_status launch_gemv_t(const WView& w, const void* x, int x_dtype, int mrows, f
     attr[0].val.programmaticStreamSerializationAllowed = 1;
     cfg.attrs = attr;
     cfg.numAttrs = 1;
-    e = cudaLaunchKernelEx(&cfg, kern, w, geo, x, x_dtype, mrows, out, ldo, device_error_word(dev));
+    e = cudaLaunchKernelEx(&cfg, kern, w, geo, x, x_dtype, mrows, out, ldo, device_error_word(dev), gp);
     if (e != cudaSuccess) return cuda_fail(e, "gemv launch");
     return cuda_fail(cudaGetLastError(), "gemv launch");
 }
@@ -655,7 +694,42 @@ jk_status launch_gemv_fmt(const WView& w, const void* x, int x_dtype, size_t m, 
     return JK_OK;
 }
 
+template <int FMT>
+jk_status launch_gemv_grouped_fmt(const WView& w, const void* x, int x_dtype, const Grp& gp, size_t max_jobs,
+                                  size_t rows, float* out, cudaStream_t stream) {
+    const int64_t est = (int64_t)(max_jobs < rows ? max_jobs : rows);
+    const unsigned y = (unsigned)max_jobs;
+    const int64_t ldo = w.n;
+    if (gp.job_rows <= 1) return launch_gemv_t<FMT, 1>(w, x, x_dtype, 1, out, ldo, stream, gp, y, est);
+    if (gp.job_rows <= 2) return launch_gemv_t<FMT, 2>(w, x, x_dtype, 2, out, ldo, stream, gp, y, est);
+    if (gp.job_rows <= 4) return launch_gemv_t<FMT, 4>(w, x, x_dtype, 4, out, ldo, stream, gp, y, est);
+    if (gp.job_rows <= 8) return launch_gemv_t<FMT, 8>(w, x, x_dtype, 8, out, ldo, stream, gp, y, est);
+    return launch_gemv_t<FMT, 16>(w, x, x_dtype, 16, out, ldo, stream, gp, y, est);
+}
+
 }  // namespace
+
+jk_status launch_gemv_grouped(const WView& w, const void* x, int x_dtype, size_t x_rows, const uint32_t* sorted,
+                              const uint32_t* offsets, const uint32_t* jobs, size_t max_jobs, uint32_t in_div,
+                              int job_rows, size_t rows, float* out, cudaStream_t stream) {
+    if (rows == 0 || max_jobs == 0) return JK_OK;
+    if (w.n % GROUP_ROWS) return fail(JK_ERR_SHAPE, "gemv: rows must be a multiple of 8");
+    if (max_jobs > 65535) return fail(JK_ERR_UNSUPPORTED, "grouped gemv: more than 65535 jobs");
+    if (job_rows < 1 || job_rows > JK_GEMV_ROWS) return fail(JK_ERR_INVALID, "grouped gemv: job rows out of range");
+    // 16 staged rows must fit the activation budget the dense path allows
+    const size_t row_bytes = (size_t)((w.k + 255) / 256) * 4 * SLOT_WORDS * 4;
+    int mr = 1;
+    while (mr < job_rows) mr <<= 1;
+    if ((size_t)mr * row_bytes > 160 * 1024) return fail(JK_ERR_UNSUPPORTED, "grouped gemv: rows too long for the job tile");
+    Grp gp{jobs, offsets, sorted, in_div, job_rows, (int64_t)x_rows};
+    switch (w.fmt) {
+    case FMT_Q4K: return launch_gemv_grouped_fmt<FMT_Q4K>(w, x, x_dtype, gp, max_jobs, rows, out, stream);
+    case FMT_Q6K: return launch_gemv_grouped_fmt<FMT_Q6K>(w, x, x_dtype, gp, max_jobs, rows, out, stream);
+    case FMT_Q8_0: return launch_gemv_grouped_fmt<FMT_Q8_0>(w, x, x_dtype, gp, max_jobs, rows, out, stream);
+    case FMT_Q5_0: return launch_gemv_grouped_fmt<FMT_Q5_0>(w, x, x_dtype, gp, max_jobs, rows, out, stream);
+    default: return launch_gemv_grouped_fmt<FMT_F16>(w, x, x_dtype, gp, max_jobs, rows, out, stream);
+    }
+}
 
 jk_status launch_gemv(const WView& w, const void* x, int x_dtype, size_t m, float* out, cudaStream_t stream) {
     if (m == 0) return JK_OK;

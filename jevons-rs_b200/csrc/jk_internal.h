@@ -69,4 +69,26 @@ jk_status launch_gemm_stream_k_fixed(const jk_qmatrix* w, const void* x, bool x_
 jk_status launch_convert_to_bf16(const void* x, int x_dtype, size_t count, void* out,
                                  cudaStream_t stream);
 
+// Expert-grouped products. The grouped GEMM runs whole tiles over (weight tile, job) pairs:
+// x_sorted holds the activation rows in expert-sorted order ([rows][k], bf16 or f16), job j covers
+// sorted rows [jobs[2j+2], min(+job_rows, offsets[e+1])) of expert e = jobs[2j+1] with weight rows
+// e*n.., and sorted row s is written to out row sorted[s] ([*, n] f32). Jobs at or past jobs[0]
+// are skipped on the device.
+jk_status launch_gemm_grouped(const jk_qmatrix* w, const void* x_sorted, bool x_bf16, size_t rows,
+                              const uint32_t* sorted, const uint32_t* offsets, const uint32_t* jobs, size_t max_jobs,
+                              int job_rows, float* out, int bt, bool pair, cudaStream_t stream);
+// Deterministic grouping of `assignments` expert ids (one CTA); experts <= GROUP_MAX_EXPERTS.
+constexpr size_t GROUP_MAX_EXPERTS = 1024;
+jk_status launch_group_experts(const uint32_t* ids, size_t assignments, size_t experts, int bm, size_t max_jobs,
+                               uint32_t* sorted, uint32_t* offsets, uint32_t* jobs, uint32_t* err,
+                               cudaStream_t stream);
+// Grouped small-row product: the GEMV over jobs of <= job_rows (<= 16) rows, grid y = max_jobs;
+// activation rows are read in place (x[sorted[s] / in_div], x_rows of them).
+jk_status launch_gemv_grouped(const WView& w, const void* x, int x_dtype, size_t x_rows, const uint32_t* sorted,
+                              const uint32_t* offsets, const uint32_t* jobs, size_t max_jobs, uint32_t in_div,
+                              int job_rows, size_t rows, float* out, cudaStream_t stream);
+// out[s] = x[sorted[s] / in_div] converted to bf16 (out_bf16) or f16; rows past x_rows become 0.
+jk_status launch_gather_rows(const void* x, int x_dtype, size_t x_rows, size_t k, const uint32_t* sorted,
+                             size_t rows, uint32_t in_div, void* out, bool out_bf16, cudaStream_t stream);
+
 }  // namespace jk

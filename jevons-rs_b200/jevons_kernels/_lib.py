@@ -30,6 +30,13 @@ class Plan(ctypes.Structure):
         return hash((self.bm, self.bn, self.splits))
 
 
+class Groups(ctypes.Structure):
+    """jk_groups: Groups (crates/jevons-kernels/src/gemm.rs:955-966) as device pointers."""
+
+    _fields_ = [("sorted", ctypes.c_void_p), ("offsets", ctypes.c_void_p), ("jobs", ctypes.c_void_p),
+                ("max_jobs", ctypes.c_size_t), ("in_div", ctypes.c_uint32), ("rows", ctypes.c_size_t)]
+
+
 SIGNATURES = {
     "jk_last_error": (ctypes.c_char_p, []),
     "jk_abi_version": (I, []),
@@ -59,6 +66,10 @@ SIGNATURES = {
     "jk_matmul_splitk_noalloc": (I, [P, P, I, S, S, P, S, I, P]),
     "jk_set_max_ctas": (I, [I, I]),
     "jk_get_max_ctas": (I, [I, ctypes.POINTER(I), ctypes.POINTER(I)]),
+    "jk_group_max_jobs": (S, [S, S, I]),
+    "jk_group_experts": (I, [I, P, S, S, I, P, P, P, S, P]),
+    "jk_matmul_grouped": (I, [P, P, I, S, ctypes.POINTER(Groups), P, S, I, I, I, P, P]),
+    "jk_matvec_grouped": (I, [P, P, I, S, ctypes.POINTER(Groups), P, S, I, P]),
 }
 
 STATUS = {0: "JK_OK", 1: "JK_ERR_INVALID", 2: "JK_ERR_UNSUPPORTED", 3: "JK_ERR_SHAPE", 4: "JK_ERR_CUDA",

@@ -18,6 +18,7 @@ import ctypes
 import numpy as np
 import torch
 
+from ._lib import Groups as _Groups
 from ._lib import JkError, Plan, check, load
 from .formats import Packed, TensorType, block, pack
 
@@ -279,6 +280,62 @@ def matmul_splitk_noalloc(gpu: Gpu, x: Buf, m: int, w: QMatrix, out: Buf, bm: in
     check(load().jk_matmul_splitk_noalloc(w.handle, xp, xt, xl, m, op, ol, int(bm), _stream()))
 
 
+class Groups:
+    """Expert grouping on the device (gemm.rs:955-966): `ids` = sorted assignment indices,
+    `offsets` [experts + 1], `jobs` [1 + 2 * max_jobs]; input row = id // in_div; `rows` output
+    rows (assignments)."""
+
+    def __init__(self, ids: Buf, offsets: Buf, jobs: Buf, max_jobs: int, in_div: int, rows: int):
+        self.ids, self.offsets, self.jobs = ids, offsets, jobs
+        self.max_jobs, self.in_div, self.rows = int(max_jobs), int(in_div), int(rows)
+
+    def _c(self) -> _Groups:
+        for b in (self.ids, self.offsets, self.jobs):
+            if b.tensor.dtype not in (torch.int32, torch.uint32) or b.tensor.device.type != "cuda":
+                raise JkError(1, "groups buffers must be 32-bit integer device buffers")
+        if self.jobs.len() < 1 + 2 * self.max_jobs or self.ids.len() < self.rows:
+            raise JkError(1, "groups buffers shorter than max_jobs / rows")
+        return _Groups(self.ids.ptr(), self.offsets.ptr(), self.jobs.ptr(), self.max_jobs, self.in_div, self.rows)
+
+
+def group_max_jobs(assignments: int, experts: int, bm: int) -> int:
+    """Job-count bound jk_group_experts needs room for: ceil(a / bm) + min(experts, a)."""
+    return int(load().jk_group_max_jobs(assignments, experts, bm))
+
+
+def group_routes(gpu: Gpu, ids: Buf, sorted_: Buf, offsets: Buf, jobs: Buf, assignments: int, experts: int,
+                 bm: int) -> None:
+    """ops::group_routes (crates/jevons-gemma4-diffusion/src/gpu/ops.rs:1100-1128): deterministic
+    grouping of `assignments` expert ids into sorted ids, offsets and jobs of `bm`-row tiles."""
+    for b in (ids, sorted_, offsets, jobs):
+        if b.tensor.dtype not in (torch.int32, torch.uint32):
+            raise JkError(1, "grouping buffers must be 32-bit integers")
+    if ids.len() < assignments or sorted_.len() < assignments or offsets.len() < experts + 1:
+        raise JkError(1, "grouping buffers too short")
+    check(load().jk_group_experts(gpu.device, ids.ptr(), assignments, experts, int(bm), sorted_.ptr(), offsets.ptr(),
+                                  jobs.ptr(), jobs.len(), _stream()))
+
+
+def matmul_grouped(gpu: Gpu, x: Buf, w: QMatrix, g: Groups, out: Buf, bm: int, bn: int = 128, splits: int = 1,
+                   scratch: SplitScratch | None = None) -> None:
+    """matmul_grouped (gemm.rs:1271-1321): each assignment row times its expert's weights on the
+    tensor cores; the jobs must have been built with tiles of `bm` rows. A scratch is required
+    (the sorted activation rows are gathered into it); one is created if none is given."""
+    if scratch is None:
+        scratch = SplitScratch(gpu)
+    gc = g._c()
+    check(load().jk_matmul_grouped(w.handle, x.ptr(), x.dtype_code(), x.len(), ctypes.byref(gc), out.ptr(),
+                                   out.len(), int(bm), int(bn), int(splits), scratch.handle, _stream()))
+
+
+def matvec_grouped(gpu: Gpu, x: Buf, w: QMatrix, g: Groups, out: Buf, mr: int) -> None:
+    """matvec_grouped (gemm.rs:1170-1200): the grouped product on the small-row kernel, jobs of
+    `mr` <= GEMV_ROWS rows."""
+    gc = g._c()
+    check(load().jk_matvec_grouped(w.handle, x.ptr(), x.dtype_code(), x.len(), ctypes.byref(gc), out.ptr(),
+                                   out.len(), int(mr), _stream()))
+
+
 def f16_linear(x: torch.Tensor, weight: torch.Tensor) -> torch.Tensor:
     """jevons_burn::kernels::f16_linear (kernels.rs:107-114): f32 x @ weight^T with FP16 weight [N, K].
 
@@ -308,4 +365,5 @@ def f16_linear_scaled(x: torch.Tensor, weight: torch.Tensor) -> torch.Tensor:
 
 
 __all__ = ["GEMV_ROWS", "Gpu", "Buf", "QMatrix", "Plan", "SplitScratch", "matmul", "matmul_plan", "matmul_tiled",
-           "matvec", "matmul_splitk_noalloc", "f16_linear", "f16_linear_scaled", "tile_n", "TensorType", "block", "pack", "JkError"]
+           "matvec", "matmul_splitk_noalloc", "Groups", "group_max_jobs", "group_routes", "matmul_grouped",
+           "matvec_grouped", "f16_linear", "f16_linear_scaled", "tile_n", "TensorType", "block", "pack", "JkError"]

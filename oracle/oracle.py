@@ -253,3 +253,48 @@ def _dequantize_words(kind: int, raw) -> np.ndarray:
             out[:, j] = d * (qv.astype(np.float32) - np.float32(16.0))
         return out.reshape(-1)
     raise OracleError("unsupported tensor type")
+
+
+# ---------------------------------------------------------------------------------------------
+# Expert grouping and grouped products
+# ---------------------------------------------------------------------------------------------
+
+def group_routes(ids, experts: int, bm: int):
+    """Restates the reference's `group` kernel (crates/jevons-gemma4-diffusion/src/gpu/ops.rs:523-585)
+    on the CPU: thread e counts the ids equal to e (:545-552), thread 0 prefix-sums the counts and
+    the bm-row tile counts (:554-567), offsets[e] = start (:569-572), the ids of expert e go to
+    consecutive positions in ascending assignment order (:573-579), and expert e's jobs are
+    (e, start + t * bm) at job_starts[e] + t (:580-584). Ids >= experts belong to no expert.
+    Returns (sorted [assignments] u32 -- positions past offsets[experts] stay 0 --,
+    offsets [experts + 1] u32, jobs [1 + 2 * njobs] u32)."""
+    ids = np.asarray(ids, dtype=np.int64).reshape(-1)
+    counts = np.array([int(np.count_nonzero(ids == e)) for e in range(experts)], dtype=np.int64)
+    starts = np.zeros(experts + 1, dtype=np.int64)
+    starts[1:] = np.cumsum(counts)
+    tiles = (counts + bm - 1) // bm
+    job_starts = np.zeros(experts + 1, dtype=np.int64)
+    job_starts[1:] = np.cumsum(tiles)
+    sorted_ = np.zeros(ids.size, dtype=np.uint32)
+    jobs = np.zeros(1 + 2 * int(job_starts[experts]), dtype=np.uint32)
+    jobs[0] = job_starts[experts]
+    for e in range(experts):
+        members = np.nonzero(ids == e)[0]
+        sorted_[starts[e]:starts[e] + members.size] = members
+        for t in range(int(tiles[e])):
+            j = int(job_starts[e]) + t
+            jobs[1 + 2 * j] = e
+            jobs[2 + 2 * j] = starts[e] + t * bm
+    return sorted_, starts.astype(np.uint32), jobs
+
+
+def matmul_grouped_f64(x: np.ndarray, w_dense: np.ndarray, n: int, ids, in_div: int) -> np.ndarray:
+    """The grouped product's definition (gemm.rs:9-11, the expected values of the reference test
+    crates/jevons-gemma4-diffusion/src/gpu/tests.rs:381-390): output row a = x[a // in_div] . W_e^T
+    with e = ids[a] and W_e = rows [e * n, (e + 1) * n) of the dequantized matrix; f64 sums."""
+    ids = np.asarray(ids, dtype=np.int64).reshape(-1)
+    x = np.ascontiguousarray(x, dtype=np.float32)
+    out = np.zeros((ids.size, n), dtype=np.float64)
+    for e in np.unique(ids):
+        rows = np.nonzero(ids == e)[0]
+        out[rows] = matmul_f64(x[rows // in_div], w_dense[e * n:(e + 1) * n])
+    return out

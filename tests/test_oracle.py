@@ -145,3 +145,67 @@ def test_bf16_round_matches_torch():
     x = np.random.default_rng(2).normal(0, 3, 4096).astype(np.float32)
     want = torch.from_numpy(x).bfloat16().float().numpy()
     assert np.array_equal(synth.bf16_round(x), want)
+
+
+# ---- expert grouping (crates/jevons-gemma4-diffusion/src/gpu/ops.rs:523-585) -----------------
+
+def test_group_oracle_known_answer():
+    # ids of 5 assignments over 3 experts: counts [2, 1, 2], starts [0, 2, 3, 5]
+    s, o, j = oracle.group_routes([2, 0, 2, 1, 0], 3, 1)
+    assert o.tolist() == [0, 2, 3, 5]
+    assert s.tolist() == [1, 4, 3, 0, 2]  # ascending assignment index within each expert
+    assert j.tolist() == [5, 0, 0, 0, 1, 1, 2, 2, 3, 2, 4]
+    s, o, j = oracle.group_routes([2, 0, 2, 1, 0], 3, 2)
+    assert j.tolist() == [3, 0, 0, 1, 2, 2, 3]
+    s, o, j = oracle.group_routes([], 4, 32)
+    assert o.tolist() == [0] * 5 and j.tolist() == [0] and s.size == 0
+
+
+@pytest.mark.parametrize("a,experts,bm", [(42, 4, 32), (300, 16, 8), (1000, 128, 1), (64, 1, 64)])
+def test_group_oracle_reference_invariants(a, experts, bm):
+    """The grouping assertions of the reference test tests.rs:338-357 hold for the oracle."""
+    ids = np.random.default_rng(a).integers(0, experts, a)
+    s, o, j = oracle.group_routes(ids, experts, bm)
+    seen = np.zeros(a, bool)
+    for e in range(experts):
+        for p in range(o[e], o[e + 1]):
+            assert ids[s[p]] == e and not seen[s[p]]
+            seen[s[p]] = True
+    assert seen.all()
+    covered = 0
+    for q in range(j[0]):
+        e, start = j[1 + 2 * q], j[2 + 2 * q]
+        assert o[e] <= start < o[e + 1]
+        covered += min(o[e + 1] - start, bm)
+    assert covered == a
+
+
+def test_group_max_jobs_bounds_every_grouping():
+    """jk_group_max_jobs (host-only, no GPU) is never below the job count of a grouping, and never
+    above the reference callers' ceil(a / bm) + experts."""
+    from jevons_kernels._lib import load
+    rng = np.random.default_rng(5)
+    for _ in range(200):
+        experts = int(rng.integers(1, 300))
+        a = int(rng.integers(0, 3000))
+        bm = int(rng.choice([1, 2, 3, 8, 16, 32, 64, 128, 256]))
+        ids = rng.integers(0, experts, a) if rng.random() < 0.5 else np.minimum(rng.geometric(0.2, a) - 1, experts - 1)
+        _, _, j = oracle.group_routes(ids, experts, bm)
+        bound = load().jk_group_max_jobs(a, experts, bm)
+        assert j[0] <= bound <= -(-a // bm) + experts
+    assert load().jk_group_max_jobs(10, 4, 0) == 0
+
+
+def test_grouped_product_definition():
+    """matmul_grouped_f64 is row a = x[a // in_div] . W_{ids[a]}^T, checked against a plain loop."""
+    rng = np.random.default_rng(9)
+    experts, n, k, tokens, top_k = 3, 5, 7, 4, 2
+    w = rng.standard_normal((experts * n, k)).astype(np.float32)
+    x = rng.standard_normal((tokens, k)).astype(np.float32)
+    ids = rng.integers(0, experts, tokens * top_k)
+    got = oracle.matmul_grouped_f64(x, w, n, ids, top_k)
+    for a in range(tokens * top_k):
+        e = ids[a]
+        for c in range(n):
+            want = sum(float(x[a // top_k, i]) * float(w[e * n + c, i]) for i in range(k))
+            assert abs(got[a, c] - want) <= 1e-12 * max(1.0, abs(want))

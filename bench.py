@@ -215,6 +215,75 @@ def run_reference(args):
 # ------------------------------------------------------------------------------------------------
 # our arm
 # ------------------------------------------------------------------------------------------------
+# Routed-expert workloads of the reference's grouped-product benchmark
+# (benchmarks/cubecl/results-routed-loop-2026-09-21/README.md, "Method"): 128 experts of Q4_K
+# gate/up weights, K=2816 -> N=1408, top-8 routes; "balanced" spreads every token's 8 routes so each
+# expert gets tokens*8/128 rows, "skewed" sends all tokens to the same 8 experts.
+G_EXPERTS, G_N, G_K, G_TOP = 128, 1408, 2816, 8
+G_WORKLOADS = [("routed_balanced_128", 128, "balanced"), ("routed_skewed_128", 128, "skewed"),
+               ("routed_balanced_512", 512, "balanced"), ("routed_skewed_512", 512, "skewed")]
+
+
+def grouped_bench(gpu, dev, timed, pk):
+    """Times grouping + grouped product per workload (the reference's timed region: grouping, job
+    construction, compute and scatter), for a small set of plans, and reports the fastest."""
+    import torch
+    from jevons_kernels import synth
+    from jevons_kernels.gemm import (Buf, Groups, QMatrix, SplitScratch, group_max_jobs, group_routes,
+                                     matmul_grouped, matvec_grouped)
+    raw = synth.q4k_blocks(np.random.default_rng(7), G_EXPERTS * G_N, G_K)
+    w = QMatrix.upload(gpu, Q4_K, G_N, G_K, G_EXPERTS, raw)
+    del raw
+    expert_bytes = G_N * G_K // 256 * 144
+    scratch = SplitScratch(gpu)
+    results = {}
+    for name, tokens, kind in G_WORKLOADS:
+        a = tokens * G_TOP
+        if kind == "balanced":
+            ids = np.array([(G_TOP * t + j) % G_EXPERTS for t in range(tokens) for j in range(G_TOP)])
+        else:
+            ids = np.tile(np.arange(G_TOP), tokens)
+        active = len(np.unique(ids))
+        per_expert = a // active
+        x = torch.from_numpy(synth.activations(np.random.default_rng(8), tokens, G_K)).to(dev).bfloat16()
+        ids_t = torch.from_numpy(ids.astype(np.int32)).to(dev)
+        out = torch.empty(a, G_N, device=dev)
+        cands = [("gemm", bm, 128) for bm in (32, 64, 128, 256) if bm // 2 < per_expert or bm == 32]
+        cands += [("gemm", bm, 256) for bm in (128, 256) if bm // 2 < per_expert]
+        if per_expert <= 16:
+            cands.append(("gemv", per_expert, 0))
+        best = None
+        tried = {}
+        for kind_p, tile, bn in cands:
+            mj = group_max_jobs(a, G_EXPERTS, tile)
+            sorted_ = torch.empty(a, dtype=torch.int32, device=dev)
+            offsets = torch.empty(G_EXPERTS + 1, dtype=torch.int32, device=dev)
+            jobs = torch.empty(1 + 2 * mj, dtype=torch.int32, device=dev)
+            g = Groups(Buf(sorted_), Buf(offsets), Buf(jobs), mj, G_TOP, a)
+
+            def call(tile=tile, bn=bn, kind_p=kind_p, g=g, sorted_=sorted_, offsets=offsets, jobs=jobs):
+                group_routes(gpu, Buf(ids_t), Buf(sorted_), Buf(offsets), Buf(jobs), a, G_EXPERTS, tile)
+                if kind_p == "gemv":
+                    matvec_grouped(gpu, Buf(x), w, g, Buf(out), tile)
+                else:
+                    matmul_grouped(gpu, Buf(x), w, g, Buf(out), tile, bn, 1, scratch)
+            steps = 50
+            ms = timed(call, steps, 3) / steps
+            label = f"{kind_p} {'mr' if kind_p == 'gemv' else 'bm'}={tile}" + (f" bn={bn}" if bn else "")
+            tried[label] = round(ms * 1e3, 2)
+            if best is None or ms < best[0]:
+                best = (ms, label)
+        ms, label = best
+        flops = 2.0 * a * G_N * G_K
+        wb = active * expert_bytes
+        results[name] = {"us": ms * 1e3, "plan": label, "tflops": flops / (ms * 1e-3) / 1e12,
+                         "weight_gbs": wb / (ms * 1e-3) / 1e9, "frac_of_hbm": wb / (ms * 1e-3) / 1e9 / pk["hbm_gbs"],
+                         "rows": a, "active_experts": active, "candidates_us": tried}
+    return {"what": "group_routes + grouped product per call (128 experts Q4_K [1408, 2816], top-8, bf16 x), "
+                    "CUDA graph replay, CUDA events; weights of the active experts stream from HBM",
+            "workloads": results}
+
+
 def run_ours(args):
     import torch
     world = int(os.environ.get("WORLD_SIZE", "1"))
@@ -366,6 +435,11 @@ def run_ours(args):
     e_ms = timed(e2e_step, args.steps, args.warmup)
     e2e_value = flops_step * world * args.steps / (e_ms * 1e-3) / 1e12
 
+    # ---- expert-grouped products (the reference's routed workloads), one GPU only -------------
+    grouped = None
+    if world == 1 and not args.no_grouped:
+        grouped = grouped_bench(gpu, dev, timed, pk)
+
     cpu = None
     if rank == 0 and world == 1 and not args.no_cpu_baseline:
         x_f32 = x.float().cpu().numpy()
@@ -393,6 +467,7 @@ def run_ours(args):
                      "algorithmic_gbs": gemv_gbs * alg_bytes / wbytes, "ms_per_product": gv_ms / gv_steps / L},
             "m32": {"metric": "Q4_K GEMM TFLOP/s (M=32, BASELINE config 1)", "value": m32_tflops, "unit": "TFLOP/s",
                     "weight_gbs": wbytes * L * gv_steps * world / (c_ms * 1e-3) / 1e9},
+            "grouped": grouped,
             "e2e": {"value": e2e_value, "unit": "TFLOP/s", "h2d_bytes_per_step": xh.numel() * 2,
                     "d2h_bytes_per_step": oh.numel() * 4},
             "gpu_launches": args.steps * L * launches_per_product,
@@ -416,6 +491,7 @@ def main():
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
     ap.add_argument("--layers", type=int, default=LAYERS)
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--no-grouped", action="store_true", help="skip the expert-grouped workloads")
     args = ap.parse_args()
     if args.warmup < 3:
         args.warmup = 3

@@ -52,14 +52,41 @@ constexpr int A_STAGE_BYTES = BW * KB * 2;
 // from that sub-partition's instruction cache and stall every MMA issue.
 //   w: 0 producer | 1 MMA | 4..7 epilogue (TMEM lane quarters 0..3) | 9 raw producer | 13 idle
 //      dequantizers 2, 3, 8, 10 (group 0) and 11, 12, 14, 15 (group 1)
-constexpr int PRODUCER_WARP = 0, MMA_WARP = 1, RAW_WARP = 9, EPI_WARP0 = 4, EPI_WARPS = 4, DQ_WARPS = 8;
+//
+// When the dequantized weights go to tensor memory instead (TMEM_A below), a warp may only write
+// the TMEM lanes of its own sub-partition (lanes 32 (w % 4) ..), so dequantizer slot s (rows
+// 32 (s % 4) ..) must sit on a warp with w % 4 == s % 4; the MMA issuer then shares its
+// sub-partition with two dequantizers:
+//   w: 0 producer | 1 MMA | 4..7 epilogue | 10 raw producer | 15 idle
+//      dequantizers 8, 9, 2, 3 (group 0) and 12, 13, 14, 11 (group 1)
+// k-blocks per MMA-issue batch (one round of barrier waits and commits per batch)
+#ifndef JK_MMA_BATCH
+constexpr int MMA_BATCH = 1;
+#else
+constexpr int MMA_BATCH = JK_MMA_BATCH;
+#endif
+constexpr int PRODUCER_WARP = 0, MMA_WARP = 1, EPI_WARP0 = 4, EPI_WARPS = 4, DQ_WARPS = 8;
 constexpr int THREADS = 512;
 constexpr int EPI_THREADS = 32 * EPI_WARPS;  // 128: 1 per weight row
+template <bool TMEM_A>
+constexpr int RAW_WARP = TMEM_A ? 10 : 9;
+template <bool TMEM_A>
 __device__ __forceinline__ int dq_slot(int warp) {  // position among the dequantizer warps, or -1
-    constexpr unsigned long long tbl = 0x76F543F2FFFF10FFull;  // nibble w: slot, F = not a dequantizer
+    // nibble w: slot, F = not a dequantizer
+    constexpr unsigned long long tbl = TMEM_A ? 0xF6547F10FFFF32FFull : 0x76F543F2FFFF10FFull;
     const int v = (int)((tbl >> (4 * warp)) & 15u);
     return v == 15 ? -1 : v;
 }
+
+// The tensor-memory table keeps every dequantizer slot on a warp of its TMEM lane quarter.
+constexpr bool tmem_slots_ok() {
+    for (int w = 0; w < 16; ++w) {
+        const int v = (int)((0xF6547F10FFFF32FFull >> (4 * w)) & 15u);
+        if (v != 15 && (v & 3) != (w & 3)) return false;
+    }
+    return true;
+}
+static_assert(tmem_slots_ok(), "dequantizer slot outside its warp's TMEM lanes");
 
 template <int FMT>
 struct RawTile {
@@ -94,16 +121,44 @@ constexpr Rings pick_rings(int b_stage, int raw_bytes) {
     return Rings{2, 2, 2};
 }
 
+// Rings when the dequantized weight stages live in tensor memory: one ring of `s` stages (each
+// stage's activation atoms in shared memory, its dequantized weights in tensor memory), at most
+// `max_stages` (the tensor memory left by the accumulators), and the raw-weight ring.
+constexpr Rings pick_rings_tmem(int b_stage, int raw_bytes, int max_stages) {
+    for (int s = max_stages < 8 ? max_stages : 8; s >= 2; --s)
+        for (int r = 8; r >= 3; --r)
+            if (s * b_stage + r * raw_bytes <= SMEM_BUDGET && (r >= s / 2 || r >= 4)) return Rings{s, s, r};
+    return Rings{2, 2, 2};
+}
+
 template <int FMT, int BT, bool PAIR = false>
 struct Smem {
-    static constexpr int B_STAGE = (PAIR ? BT / 2 : BT) * 128;  // a pair CTA holds half the activation rows
+    // Dequantized weight stages in tensor memory (written with tcgen05.st, read by the MMA as its
+    // A operand) where the two accumulator buffers leave room for them: single CTAs with BT <= 128.
+    // This keeps the 16 KB per k-block of dequantized weights off the shared-memory pipe twice
+    // (the dequantizers' stores and the MMA's reads). A TMEM_A stage holds KPS = 2 k-blocks (one
+    // per dequantizer group) and one barrier pair serves the activations and the weights of the
+    // stage: the MMA issuer then waits and commits once per two k-blocks (an mbarrier wait costs
+    // about as much issue time as four M=128, N=32 MMAs).
+    static constexpr bool TMEM_A = FMT != FMT_F16 && !PAIR && BT <= 128;
+#ifndef JK_KPS
+    static constexpr int KPS = TMEM_A ? 4 : 1;                  // k-blocks per stage
+#else
+    static constexpr int KPS = TMEM_A ? JK_KPS : 1;
+#endif
+    static constexpr int B_ATOM = (PAIR ? BT / 2 : BT) * 128;  // one k-block of activations (a pair CTA: half the rows)
+    static constexpr int B_STAGE = KPS * B_ATOM;
     static constexpr int raw_bytes = RawTile<FMT>::bytes;
-    static constexpr Rings rings = pick_rings(B_STAGE, raw_bytes);
+    static constexpr uint32_t TMEM_A0 = 2 * BT;  // first tensor-memory column of the A stages
+    static constexpr Rings rings = TMEM_A ? pick_rings_tmem(B_STAGE, raw_bytes, (512 - 2 * BT) / (32 * KPS))
+                                          : pick_rings(B_STAGE, raw_bytes);
     static constexpr int SX = rings.sx, SA = rings.sa, R = rings.r;
     static_assert(FMT != FMT_F16 || SX == SA, "FP16 weights share the activation ring");
+    static constexpr uint32_t TMEM_COLS = TMEM_A ? 512 : 2 * BT;
+    static_assert(!TMEM_A || (SX == SA && TMEM_A0 + 32 * KPS * SA <= TMEM_COLS), "tensor memory budget");
     static constexpr int off_b = 0;
     static constexpr int off_a = off_b + SX * B_STAGE;
-    static constexpr int off_raw = off_a + SA * A_STAGE_BYTES;
+    static constexpr int off_raw = off_a + (TMEM_A ? 0 : SA * A_STAGE_BYTES);
     static constexpr int off_bar = off_raw + R * raw_bytes;
     // Stream-K fix-up: an owner's final segment is the CTA's last, so by then the operand and raw
     // stages [0, off_bar) are idle. They hold a ring of FIX_NB chunks for the contributor partials
@@ -308,14 +363,31 @@ __device__ __forceinline__ void tmem_ld16(uint32_t taddr, uint32_t (&v)[16]) {
 //   Q4_K part p: qs bytes 32j + 16p .. +16 -> low-nibble chunks 2p, 2p+1 and high-nibble chunks
 //                2p+4, 2p+5 of k-block j (sub-blocks 2j and 2j+1)
 //   others part p: chunks 4p .. 4p+3 of k-block j
-template <bool BF16>
-__device__ __forceinline__ void store_chunk8(uint8_t* arow, int sw, int c, const float (&v)[8]) {
+// Destinations of a dequantized weight row's k-block (8 chunks of 8 16-bit values, k order):
+// SmemRow writes the row of a 128-byte swizzled shared-memory A stage; RegRow keeps the 32 words in
+// registers for one tcgen05.st into a tensor-memory A stage.
+struct SmemRow {
+    uint8_t* arow;
+    int sw;
+    __device__ __forceinline__ void put(int c, uint4 v) { *reinterpret_cast<uint4*>(arow + 16 * (c ^ sw)) = v; }
+};
+struct RegRow {
+    uint32_t w[32];
+    __device__ __forceinline__ void put(int c, uint4 v) {
+        w[4 * c] = v.x;
+        w[4 * c + 1] = v.y;
+        w[4 * c + 2] = v.z;
+        w[4 * c + 3] = v.w;
+    }
+};
+template <bool BF16, class O>
+__device__ __forceinline__ void put8(O& o, int c, const float (&v)[8]) {
     uint4 pk;
     pk.x = pack2<BF16>(v[0], v[1]);
     pk.y = pack2<BF16>(v[2], v[3]);
     pk.z = pack2<BF16>(v[4], v[5]);
     pk.w = pack2<BF16>(v[6], v[7]);
-    *reinterpret_cast<uint4*>(arow + 16 * (c ^ sw)) = pk;
+    o.put(c, pk);
 }
 
 // 8 exact values (d*sc)*q - dmin*m (as fma, see jk_decode.cuh) of the 4 nibble-bytes of w0, w1
@@ -397,29 +469,25 @@ struct SbDequant<FMT_Q4K, BF16> {
             }
         }
     }
-    template <int J, int PART>
-    __device__ __forceinline__ void kblock(const uint8_t* raw_row, int, uint8_t* arow, int sw) {
+    template <int J, int PART, class O>
+    __device__ __forceinline__ void kblock(const uint8_t* raw_row, int, int, O& o) {
         const uint4 q = *reinterpret_cast<const uint4*>(raw_row + 16 + 32 * J + 16 * PART);
         if constexpr (BF16) {
             const uint32_t dlo = dd2[2 * J], mlo = nmm2[2 * J], dhi = dd2[2 * J + 1], mhi = nmm2[2 * J + 1];
-            *reinterpret_cast<uint4*>(arow + 16 * ((2 * PART) ^ sw)) =
-                q4k_pack8<true>(q.x & 0x0F0F0F0Fu, q.y & 0x0F0F0F0Fu, dlo, mlo);
-            *reinterpret_cast<uint4*>(arow + 16 * ((2 * PART + 1) ^ sw)) =
-                q4k_pack8<true>(q.z & 0x0F0F0F0Fu, q.w & 0x0F0F0F0Fu, dlo, mlo);
-            *reinterpret_cast<uint4*>(arow + 16 * ((2 * PART + 4) ^ sw)) =
-                q4k_pack8<true>((q.x >> 4) & 0x0F0F0F0Fu, (q.y >> 4) & 0x0F0F0F0Fu, dhi, mhi);
-            *reinterpret_cast<uint4*>(arow + 16 * ((2 * PART + 5) ^ sw)) =
-                q4k_pack8<true>((q.z >> 4) & 0x0F0F0F0Fu, (q.w >> 4) & 0x0F0F0F0Fu, dhi, mhi);
+            o.put(2 * PART, q4k_pack8<true>(q.x & 0x0F0F0F0Fu, q.y & 0x0F0F0F0Fu, dlo, mlo));
+            o.put(2 * PART + 1, q4k_pack8<true>(q.z & 0x0F0F0F0Fu, q.w & 0x0F0F0F0Fu, dlo, mlo));
+            o.put(2 * PART + 4, q4k_pack8<true>((q.x >> 4) & 0x0F0F0F0Fu, (q.y >> 4) & 0x0F0F0F0Fu, dhi, mhi));
+            o.put(2 * PART + 5, q4k_pack8<true>((q.z >> 4) & 0x0F0F0F0Fu, (q.w >> 4) & 0x0F0F0F0Fu, dhi, mhi));
         } else {
             float v[8];
             q4k_vals(q.x & 0x0F0F0F0Fu, q.y & 0x0F0F0F0Fu, dd[2 * J], mm[2 * J], v);
-            store_chunk8<false>(arow, sw, 2 * PART, v);
+            put8<false>(o, 2 * PART, v);
             q4k_vals(q.z & 0x0F0F0F0Fu, q.w & 0x0F0F0F0Fu, dd[2 * J], mm[2 * J], v);
-            store_chunk8<false>(arow, sw, 2 * PART + 1, v);
+            put8<false>(o, 2 * PART + 1, v);
             q4k_vals((q.x >> 4) & 0x0F0F0F0Fu, (q.y >> 4) & 0x0F0F0F0Fu, dd[2 * J + 1], mm[2 * J + 1], v);
-            store_chunk8<false>(arow, sw, 2 * PART + 4, v);
+            put8<false>(o, 2 * PART + 4, v);
             q4k_vals((q.z >> 4) & 0x0F0F0F0Fu, (q.w >> 4) & 0x0F0F0F0Fu, dd[2 * J + 1], mm[2 * J + 1], v);
-            store_chunk8<false>(arow, sw, 2 * PART + 5, v);
+            put8<false>(o, 2 * PART + 5, v);
         }
     }
 };
@@ -434,15 +502,15 @@ struct SbDequant<FMT_Q6K, BF16> {
     __device__ __forceinline__ void begin(const uint8_t*, const WView&, int64_t, bool row_ok, int) {
         d = row_ok ? half_bits_to_float(d_next) : 0.f;
     }
-    template <int J, int PART>
-    __device__ __forceinline__ void kblock(const uint8_t* body, int, uint8_t* arow, int sw) {
+    template <int J, int PART, class O>
+    __device__ __forceinline__ void kblock(const uint8_t* body, int, int, O& o) {
         Q6KBlock bq;
         bq.load(body, d, J);
         float v[8];
 #pragma unroll
         for (int i = 0; i < 4; ++i) {
             bq.chunk(4 * PART + i, v);
-            store_chunk8<BF16>(arow, sw, 4 * PART + i, v);
+            put8<BF16>(o, 4 * PART + i, v);
         }
     }
 };
@@ -466,8 +534,8 @@ struct SbDequant<FMT_Q8_0, BF16> {
     __device__ __forceinline__ void begin(const uint8_t*, const WView&, int64_t, bool row_ok, int) {
         dcur = row_ok ? d_next : make_uint4(0, 0, 0, 0);
     }
-    template <int J, int PART>
-    __device__ __forceinline__ void kblock(const uint8_t* raw_row_half0, int row, uint8_t* arow, int sw) {
+    template <int J, int PART, class O>
+    __device__ __forceinline__ void kblock(const uint8_t* raw_row_half0, int row, int, O& o) {
         // k-block J: 128-byte swizzled half J/2 of the stage (the caller points raw_row_half0 at
         // half 0's row; half 1 starts BW * 128 bytes later), logical chunks 4 (J%2) ..
         const uint32_t dw = (J >> 1) == 0 ? ((J & 1) ? dcur.y : dcur.x) : ((J & 1) ? dcur.w : dcur.z);
@@ -478,7 +546,7 @@ struct SbDequant<FMT_Q8_0, BF16> {
 #pragma unroll
         for (int i = 0; i < 4; ++i) {
             bq.chunk(4 * PART + i, v);
-            store_chunk8<BF16>(arow, sw, 4 * PART + i, v);
+            put8<BF16>(o, 4 * PART + i, v);
         }
     }
 };
@@ -505,8 +573,8 @@ struct SbDequant<FMT_Q5_0, BF16> {
         h0 = h_next0;
         h1 = h_next1;
     }
-    template <int J, int PART>
-    __device__ __forceinline__ void kblock(const uint8_t* rowp, int, uint8_t* arow, int sw) {
+    template <int J, int PART, class O>
+    __device__ __forceinline__ void kblock(const uint8_t* rowp, int, int sw, O& o) {
         // 128-byte swizzled row of the super-block; k-block J = logical chunks 2J, 2J+1
         const uint32_t dw = (J >> 1) == 0 ? ((J & 1) ? dcur.y : dcur.x) : ((J & 1) ? dcur.w : dcur.z);
         const uint32_t ha = J == 0 ? h0.x : J == 1 ? h0.z : J == 2 ? h1.x : h1.z;
@@ -519,7 +587,7 @@ struct SbDequant<FMT_Q5_0, BF16> {
 #pragma unroll
         for (int i = 0; i < 4; ++i) {
             bq.chunk(4 * PART + i, v);
-            store_chunk8<BF16>(arow, sw, 4 * PART + i, v);
+            put8<BF16>(o, 4 * PART + i, v);
         }
     }
 };
@@ -569,19 +637,95 @@ __device__ __forceinline__ void dequant_role(const Sched& sched, SegState& ss, u
                 if (it0 >= SA) ok = __all_sync(0xFFFFFFFFu, mbar_wait(empty_a(s), ((it0 / SA) - 1) & 1, err));
                 if (!ok) break;
                 JK_TRACE_POINT(6, it0);
-                uint8_t* arow = smem + L::off_a + s * A_STAGE_BYTES + row_in_tile * 128;
-                switch (j) {
-                case 0: dq.template kblock<0, 0>(raw_row, row_in_tile, arow, sw); dq.template kblock<0, 1>(raw_row, row_in_tile, arow, sw); break;
-                case 1: dq.template kblock<1, 0>(raw_row, row_in_tile, arow, sw); dq.template kblock<1, 1>(raw_row, row_in_tile, arow, sw); break;
-                case 2: dq.template kblock<2, 0>(raw_row, row_in_tile, arow, sw); dq.template kblock<2, 1>(raw_row, row_in_tile, arow, sw); break;
-                default: dq.template kblock<3, 0>(raw_row, row_in_tile, arow, sw); dq.template kblock<3, 1>(raw_row, row_in_tile, arow, sw); break;
+                {
+                    SmemRow o{smem + L::off_a + s * A_STAGE_BYTES + row_in_tile * 128, sw};
+                    switch (j) {
+                    case 0: dq.template kblock<0, 0>(raw_row, row_in_tile, sw, o); dq.template kblock<0, 1>(raw_row, row_in_tile, sw, o); break;
+                    case 1: dq.template kblock<1, 0>(raw_row, row_in_tile, sw, o); dq.template kblock<1, 1>(raw_row, row_in_tile, sw, o); break;
+                    case 2: dq.template kblock<2, 0>(raw_row, row_in_tile, sw, o); dq.template kblock<2, 1>(raw_row, row_in_tile, sw, o); break;
+                    default: dq.template kblock<3, 0>(raw_row, row_in_tile, sw, o); dq.template kblock<3, 1>(raw_row, row_in_tile, sw, o); break;
+                    }
+                    fence_proxy_async_smem();
                 }
-                fence_proxy_async_smem();
                 __syncwarp();
                 JK_TRACE_POINT(9, it0);
                 if (lane == 0) {
                     if constexpr (PAIR) mbar_arrive_cluster(mapa_shared(full_a(s), 0));  // the leader issues the MMA
                     else mbar_arrive(full_a(s));
+                }
+            }
+            if (!ok) break;
+            __syncwarp();
+            if (lane == 0) mbar_arrive(raw_empty(slot));
+        }
+    }
+}
+
+// Dequantizer role with tensor-memory A stages (Smem::TMEM_A): group g decodes the k-blocks
+// kb with kb % 2 == g into TMEM lanes of its rows (one tcgen05.st of 32 columns per k-block);
+// both groups wait for a stage to be free and arrive on its full barrier once per stage, whether
+// or not the stage holds a k-block of theirs (a segment's edge stages may hold one k-block).
+template <int FMT, bool BF16, int BT>
+__device__ __forceinline__ void dequant_role_tmem(const Sched& sched, SegState& ss, uint8_t* smem, int row_in_tile,
+                                                  int grp, const WView& w, uint32_t* err, bool& ok, uint32_t bar0,
+                                                  int lane, uint32_t tmem) {
+    using L = Smem<FMT, BT, false>;
+    constexpr int S = L::SX, R = L::R, KPS = L::KPS;
+    static_assert(KPS % 2 == 0, "the two dequantizer groups alternate k-blocks within a stage");
+    auto full = [&](int st) { return bar0 + 8u * (L::bar_full_b + st); };
+    auto empty = [&](int st) { return bar0 + 8u * (L::bar_empty_b + st); };
+    auto raw_full = [&](int r) { return bar0 + 8u * (L::bar_raw_full + r); };
+    auto raw_empty = [&](int r) { return bar0 + 8u * (L::bar_raw_empty + r); };
+    const int sw = row_in_tile & 7;
+    const uint32_t tlanes = tmem + ((uint32_t)(row_in_tile & ~31) << 16) + L::TMEM_A0;
+    SbDequant<FMT, BF16> dq;
+    int st = 0, raw_n = 0;
+    Seg sg;
+    while (ok && seg_next(sched, ss, sg)) {
+        const int64_t row = tile_at<BW, BT>(sched, sg.tile, 0, 0).wrow0 + row_in_tile;
+        const bool row_ok = row < w.rows;
+        const int64_t rr = row_ok ? row : 0;
+        const int sb_lo = sg.kb_lo >> 2, sb_hi = (sg.kb_hi - 1) >> 2;
+        dq.prefetch(w, rr, sb_lo);
+        for (int sb = sb_lo; sb <= sb_hi && ok; ++sb) {
+            const int r = raw_n++;
+            const int slot = r % R;
+            ok = __all_sync(0xFFFFFFFFu, mbar_wait(raw_full(slot), (r / R) & 1, err));
+            if (!ok) break;
+            JK_TRACE_POINT(10, r);
+            const uint8_t* raw_row = smem + L::off_raw + slot * L::raw_bytes +
+                                     row_in_tile * (FMT == FMT_Q4K ? 144 : FMT == FMT_Q6K ? 208 : 128);
+            dq.begin(raw_row, w, rr, row_ok, sb);
+            if (sb < sb_hi) dq.prefetch(w, rr, sb + 1);
+            JK_TRACE_POINT(11, r);
+#pragma unroll
+            for (int j = 0; j < 4; ++j) {
+                const int kb = 4 * sb + j;
+                if (kb < sg.kb_lo || kb >= sg.kb_hi) continue;
+                const int s = st % S;
+                if (kb == sg.kb_lo || kb % KPS == 0) {  // the stage's first k-block: wait until it is free
+                    if (st >= S) ok = __all_sync(0xFFFFFFFFu, mbar_wait(empty(s), ((st / S) - 1) & 1, err));
+                    if (!ok) break;
+                    JK_TRACE_POINT(6, st);
+                    tc_fence_after();  // the MMAs that read the stage before have completed
+                }
+                if ((kb & 1) == grp) {
+                    RegRow o;
+                    switch (j) {
+                    case 0: dq.template kblock<0, 0>(raw_row, row_in_tile, sw, o); dq.template kblock<0, 1>(raw_row, row_in_tile, sw, o); break;
+                    case 1: dq.template kblock<1, 0>(raw_row, row_in_tile, sw, o); dq.template kblock<1, 1>(raw_row, row_in_tile, sw, o); break;
+                    case 2: dq.template kblock<2, 0>(raw_row, row_in_tile, sw, o); dq.template kblock<2, 1>(raw_row, row_in_tile, sw, o); break;
+                    default: dq.template kblock<3, 0>(raw_row, row_in_tile, sw, o); dq.template kblock<3, 1>(raw_row, row_in_tile, sw, o); break;
+                    }
+                    tmem_st32(tlanes + (uint32_t)(32 * (KPS * s + kb % KPS)), o.w);
+                }
+                if (kb == sg.kb_hi - 1 || kb % KPS == KPS - 1) {  // the stage's last k-block: publish it
+                    tmem_st_wait();
+                    tc_fence_before();
+                    __syncwarp();
+                    JK_TRACE_POINT(9, st);
+                    if (lane == 0) mbar_arrive(full(s));
+                    ++st;
                 }
             }
             if (!ok) break;
@@ -606,7 +750,7 @@ gemm_tc_kernel(const __grid_constant__ CUtensorMap tm_x, const __grid_constant__
     constexpr bool QUANT = FMT != FMT_F16;
     static_assert(!PAIR || QUANT, "pairs are for quantized weights");
     constexpr int TW = PAIR ? 2 * BW : BW;  // weight rows per tile
-    constexpr uint32_t TMEM_COLS = 2 * BT;
+    constexpr uint32_t TMEM_COLS = L::TMEM_COLS;
     constexpr uint32_t IDESC = idesc_f16(BF16, TW, BT);
 
     extern __shared__ uint8_t smem_raw[];
@@ -634,7 +778,8 @@ gemm_tc_kernel(const __grid_constant__ CUtensorMap tm_x, const __grid_constant__
 
     if (threadIdx.x == 0) {
         for (int s = 0; s < SX; ++s) {
-            mbar_init(full_b(s), 1);
+            // TMEM_A: the stage's producer arrival (with its bytes) and every dequantizer warp
+            mbar_init(full_b(s), L::TMEM_A ? 1 + DQ_WARPS : 1);
             mbar_init(empty_b(s), 1);
         }
         for (int s = 0; s < SA; ++s) {
@@ -685,6 +830,28 @@ gemm_tc_kernel(const __grid_constant__ CUtensorMap tm_x, const __grid_constant__
             tma_prefetch(&tm_w);
         }
         int it = 0;
+        if constexpr (L::TMEM_A) {
+            constexpr int KPS = L::KPS;
+            while (ok && seg_next(sched, ss, sg)) {
+                const int32_t m0 = (int32_t)tile_at<TW, BT>(sched, sg.tile, rank, m).m0;
+                for (int p = sg.kb_lo / KPS; p <= (sg.kb_hi - 1) / KPS && ok; ++p) {
+                    const int s = it % SX;
+                    if (it >= SX) ok = __all_sync(0xFFFFFFFFu, mbar_wait(empty_b(s), ((it / SX) - 1) & 1, err));
+                    if (!ok) break;
+                    JK_TRACE_POINT(1, it);
+                    const int lo = p * KPS > sg.kb_lo ? p * KPS : sg.kb_lo;
+                    const int hi = p * KPS + KPS < sg.kb_hi ? p * KPS + KPS : sg.kb_hi;
+                    if (elect_one()) {
+                        mbar_expect_tx(full_b(s), (uint32_t)((hi - lo) * L::B_ATOM));
+                        for (int kb = lo; kb < hi; ++kb)
+                            tma_load_2d(sbase + L::off_b + s * L::B_STAGE + (kb % KPS) * L::B_ATOM, &tm_x, kb * KB, m0,
+                                        full_b(s));
+                    }
+                    __syncwarp();
+                    ++it;
+                }
+            }
+        } else
         while (ok && seg_next(sched, ss, sg)) {
             const TileAt ta = tile_at<TW, BT>(sched, sg.tile, rank, m);
             const int32_t n0 = (int32_t)ta.wrow0;
@@ -696,12 +863,12 @@ gemm_tc_kernel(const __grid_constant__ CUtensorMap tm_x, const __grid_constant__
                 JK_TRACE_POINT(1, it);
                 if constexpr (PAIR) {
                     // both halves count on the leader's full barrier; only the leader expects them
-                    if (leader) {
+                    if (elect_one()) {
                         if (rank == 0) mbar_expect_tx(full_b(s), 2 * L::B_STAGE);
                         tma_load_2d_pair(sbase + L::off_b + s * L::B_STAGE, &tm_x, kb * KB, m0,
                                          mapa_shared(full_b(s), 0));
                     }
-                } else if (leader) {
+                } else if (elect_one()) {
                     if constexpr (FMT == FMT_F16) {
                         mbar_expect_tx(full_b(s), L::B_STAGE + A_STAGE_BYTES);
                         tma_load_2d(sbase + L::off_a + s * A_STAGE_BYTES, &tm_w, kb * KB, n0, full_b(s));
@@ -718,7 +885,7 @@ gemm_tc_kernel(const __grid_constant__ CUtensorMap tm_x, const __grid_constant__
         // complete on the leader's barrier; the final cluster barrier covers them)
         if (!ok && (!PAIR || rank == 0))
             for (int i = it - SX < 0 ? 0 : it - SX; i < it; ++i) mbar_wait(full_b(i % SX), (i / SX) & 1, err);
-    } else if (warp == RAW_WARP) {
+    } else if (warp == RAW_WARP<L::TMEM_A>) {
         // --------------------- raw weight producer: runs up to R super-blocks ahead ---------------------
         if constexpr (QUANT) {
             int raw_n = 0;
@@ -734,7 +901,7 @@ gemm_tc_kernel(const __grid_constant__ CUtensorMap tm_x, const __grid_constant__
                     JK_TRACE_POINT(2, r);
                     const int sb = kb >> 2;
                     const uint32_t dst = sbase + L::off_raw + slot * L::raw_bytes;
-                    if (leader) {
+                    if (elect_one()) {
                         mbar_expect_tx(raw_full(slot), L::raw_bytes);
                         if constexpr (FMT == FMT_Q4K) {
                             tma_load_2d(dst, &tm_w, sb * 36, n0, raw_full(slot));
@@ -767,33 +934,91 @@ gemm_tc_kernel(const __grid_constant__ CUtensorMap tm_x, const __grid_constant__
             if (!ok) break;
             tc_fence_after();
             const uint32_t acc = tmem + (uint32_t)(b * BT);
-            for (int kb = sg.kb_lo; kb < sg.kb_hi; ++kb, ++it) {
-                const int sx = it % SX, sa = it % SA;
-                bool got = mbar_wait(full_b(sx), (uint32_t)((it / SX) & 1), err);
-                JK_TRACE_POINT(3, it);
-                if (got && QUANT) got = mbar_wait(full_a(sa), (uint32_t)((it / SA) & 1), err);
+            if constexpr (L::TMEM_A) {
+                // one wait and one commit per stage of KPS k-blocks; A from tensor memory (8 columns
+                // = 16 values per lane per K=16 step), B from the stage's activation atoms
+                constexpr int KPS = L::KPS;
+                for (int p = sg.kb_lo / KPS; p <= (sg.kb_hi - 1) / KPS; ++p) {
+                    const int s = it % SX;
+                    JK_TRACE_POINT(2, it);
+                    ok = __all_sync(0xFFFFFFFFu, mbar_wait(full_b(s), (uint32_t)((it / SX) & 1), err));
+                    if (!ok) break;
+                    JK_TRACE_POINT(4, it);
+                    tc_fence_after();
+                    // Operands are computed by the whole (converged) warp and one elected lane issues:
+                    // warp-uniform descriptors let the MMAs go out back to back (from a lane-0 branch
+                    // each MMA costs about twice its tensor-pipe time at N = 32).
+                    const uint32_t at = tmem + L::TMEM_A0 + (uint32_t)(32 * KPS * s);
+                    const uint64_t bd = sw128_kmajor_desc(sbase + L::off_b + s * L::B_STAGE);
+                    if (elect_one()) {
+#pragma unroll
+                        for (int j = 0; j < KPS; ++j) {
+                            const int kb = p * KPS + j;
+                            if (kb < sg.kb_lo || kb >= sg.kb_hi) continue;
+#pragma unroll
+                            for (int k = 0; k < KB / 16; ++k)
+                                mma_f16_ta(acc, at + (uint32_t)(32 * j + 8 * k), bd + (uint64_t)(j * (L::B_ATOM >> 4) + 2 * k),
+                                           IDESC, (kb > sg.kb_lo || k > 0) ? 1u : 0u);
+                        }
+                        JK_TRACE_POINT(0, it);
+                        commit(empty_b(s));
+                    }
+                    __syncwarp();
+                    issued = true;
+                    ++it;
+                }
+            } else
+            // k-blocks go to the tensor pipe MMA_BATCH at a time: the waits, commits and loop
+            // overhead of a batch are paid once while the previous batch's MMAs execute
+            for (int kb = sg.kb_lo; kb < sg.kb_hi;) {
+                const int nb = kb + MMA_BATCH <= sg.kb_hi ? MMA_BATCH : sg.kb_hi - kb;
+                JK_TRACE_POINT(2, it);
+                bool got = true;
+#pragma unroll
+                for (int q = 0; q < MMA_BATCH; ++q) {
+                    if (q < nb && got) got = mbar_wait(full_b((it + q) % SX), (uint32_t)(((it + q) / SX) & 1), err);
+                    if (q < nb && got && QUANT) got = mbar_wait(full_a((it + q) % SA), (uint32_t)(((it + q) / SA) & 1), err);
+                }
                 ok = __all_sync(0xFFFFFFFFu, got);
                 if (!ok) break;
                 JK_TRACE_POINT(4, it);
                 tc_fence_after();
-                const uint64_t ad = sw128_kmajor_desc(sbase + L::off_a + sa * A_STAGE_BYTES);
-                const uint64_t bd = sw128_kmajor_desc(sbase + L::off_b + sx * L::B_STAGE);
-                if (leader) {
+                uint64_t bdq[MMA_BATCH], adq[MMA_BATCH];
 #pragma unroll
-                    for (int k = 0; k < KB / 16; ++k) {  // +32 bytes per K=16 step inside the swizzle atom
-                        if constexpr (PAIR)
-                            mma_f16_pair(acc, ad + 2u * k, bd + 2u * k, IDESC, (kb > sg.kb_lo || k > 0) ? 1u : 0u);
-                        else
-                            mma_f16(acc, ad + 2u * k, bd + 2u * k, IDESC, (kb > sg.kb_lo || k > 0) ? 1u : 0u);
+                for (int q = 0; q < MMA_BATCH; ++q) {
+                    bdq[q] = sw128_kmajor_desc(sbase + L::off_b + ((it + q) % SX) * L::B_STAGE);
+                    adq[q] = sw128_kmajor_desc(sbase + L::off_a + ((it + q) % SA) * A_STAGE_BYTES);
+                }
+                if (elect_one()) {
+#pragma unroll
+                    for (int q = 0; q < MMA_BATCH; ++q) {
+                        if (q >= nb) break;
+                        const uint64_t bd = bdq[q], ad = adq[q];
+#pragma unroll
+                        for (int k = 0; k < KB / 16; ++k) {  // +32 bytes per K=16 step inside the swizzle atom
+                            const uint32_t accum = (kb + q > sg.kb_lo || k > 0) ? 1u : 0u;
+                            if constexpr (PAIR)
+                                mma_f16_pair(acc, ad + 2u * k, bd + 2u * k, IDESC, accum);
+                            else
+                                mma_f16(acc, ad + 2u * k, bd + 2u * k, IDESC, accum);
+                        }
                     }
-                    commit(empty_b(sx));
-                    if constexpr (QUANT) commit(empty_a(sa));
+                    JK_TRACE_POINT(0, it);
+#pragma unroll
+                    for (int q = 0; q < MMA_BATCH; ++q) {
+                        if (q >= nb) break;
+                        commit(empty_b((it + q) % SX));
+                        if constexpr (QUANT) commit(empty_a((it + q) % SA));
+                    }
+                    JK_TRACE_POINT(1, it);
                 }
                 __syncwarp();
                 issued = true;
+                kb += nb;
+                it += nb;
             }
             if (!ok) break;
-            if (leader) commit(acc_full(b));  // arrives when this segment's MMAs are complete
+            if (elect_one()) commit(acc_full(b));  // arrives when this segment's MMAs are complete
             __syncwarp();
             JK_TRACE_POINT(12, seg_i);
             ++seg_i;
@@ -1001,12 +1226,15 @@ gemm_tc_kernel(const __grid_constant__ CUtensorMap tm_x, const __grid_constant__
             }
             ++seg_i;
         }
-    } else if (dq_slot(warp) >= 0) {
+    } else if (dq_slot<L::TMEM_A>(warp) >= 0) {
         // ------------------------------ dequantizers ------------------------------
         if constexpr (QUANT) {
-            const int t = 32 * dq_slot(warp) + lane;  // 0..255
+            const int t = 32 * dq_slot<L::TMEM_A>(warp) + lane;  // 0..255
             const int row_in_tile = t & (BW - 1);
-            dequant_role<FMT, BF16, BT, PAIR>(sched, ss, smem, row_in_tile, t / BW, rank, w, err, ok, bar0, lane);
+            if constexpr (L::TMEM_A)
+                dequant_role_tmem<FMT, BF16, BT>(sched, ss, smem, row_in_tile, t / BW, w, err, ok, bar0, lane, tmem);
+            else
+                dequant_role<FMT, BF16, BT, PAIR>(sched, ss, smem, row_in_tile, t / BW, rank, w, err, ok, bar0, lane);
         }
     }
 

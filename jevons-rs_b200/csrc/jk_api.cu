@@ -5,7 +5,7 @@
 //   TensorType::block            crates/jevons-formats/src/gguf.rs:134-145
 //   quant::{q4k_scale_min, packed_words, pack}   crates/jevons-formats/src/quant.rs:14-23,128-193
 //   QMatrix::{upload, from_packed, f16_view}     crates/jevons-kernels/src/gemm.rs:832-948
-//   Plan::{heuristic, valid_for}, choose_splits  gemm.rs:981-1038
+//   Plan::{heuristic, valid_for}                 gemm.rs:981-1038
 //   matmul / matmul_plan / matvec / matmul_tiled gemm.rs:1067-1168
 //   SplitScratch                                 gemm.rs:1040-1065
 //   f16_linear / plan                            crates/jevons-burn/src/kernels.rs:16-31,47-114
@@ -645,14 +645,6 @@ int row_tile_for(size_t m) {
     return 256;
 }
 
-// choose_splits (gemm.rs:1031-1038): double the split-K factor until the tile count reaches the
-// target, keeping >= 4 k-steps per slice.
-int choose_splits(size_t base, size_t steps, size_t target) {
-    int splits = 1;
-    while (splits < 16 && base * (size_t)splits < target && steps / ((size_t)splits * 2) >= 4) splits *= 2;
-    return splits;
-}
-
 bool plan_valid(const jk_plan& p, const jk_qmatrix* w, size_t m) {
     if (p.bm == 0) return m <= JK_GEMV_ROWS && p.splits == 1 && w->k / 32 <= 1u << 20;
     const bool bm_ok = p.bm == 32 || p.bm == 64 || p.bm == 128 || p.bm == 256;
@@ -687,9 +679,15 @@ jk::WView dense_view(const jk_qmatrix* w) {
 
 }  // namespace
 
+// Plan::heuristic (gemm.rs:989-1004), adapted to this kernel: the activation-row tile grows with
+// m but stops at 128 for block-quantized weights (there the dequantized weights live in tensor
+// memory next to two 128-column accumulators, which measures faster than 256-row tiles with
+// shared-memory weight stages); split-K (`splits > 1`, the stream-K schedule) is chosen when whole
+// tiles would leave more than a quarter of the last wave's SMs idle.
 extern "C" jk_status jk_plan_heuristic(const jk_qmatrix* w, size_t m, int row_invariant, int sms, jk_plan* out) {
     if (!w || !out) return fail(JK_ERR_INVALID, "null pointer");
-    const int bm = row_tile_for(m);
+    int bm = row_tile_for(m);
+    if (w->type != JK_TYPE_F16 && bm > 128) bm = 128;
     const int bn = 128;
     if (row_invariant) {
         *out = {bm, bn, 1};
@@ -700,8 +698,10 @@ extern "C" jk_status jk_plan_heuristic(const jk_qmatrix* w, size_t m, int row_in
         return JK_OK;
     }
     const size_t target = sms > 0 ? (size_t)sms : (size_t)jk::sm_count(w->device);
-    const size_t base = (w->n + 127) / 128 * ((m + bm - 1) / bm);
-    *out = {bm, bn, choose_splits(base, w->k / 64, target)};
+    const size_t tiles = (w->n + 127) / 128 * ((m + bm - 1) / bm);
+    const size_t waves = (tiles + target - 1) / target;
+    const bool balanced = tiles * 4 >= waves * target * 3;
+    *out = {bm, bn, balanced || w->k / 64 < 2 ? 1 : 2};
     return JK_OK;
 }
 

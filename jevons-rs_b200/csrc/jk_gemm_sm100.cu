@@ -136,16 +136,13 @@ struct Smem {
     // Dequantized weight stages in tensor memory (written with tcgen05.st, read by the MMA as its
     // A operand) where the two accumulator buffers leave room for them: single CTAs with BT <= 128.
     // This keeps the 16 KB per k-block of dequantized weights off the shared-memory pipe twice
-    // (the dequantizers' stores and the MMA's reads). A TMEM_A stage holds KPS = 2 k-blocks (one
-    // per dequantizer group) and one barrier pair serves the activations and the weights of the
-    // stage: the MMA issuer then waits and commits once per two k-blocks (an mbarrier wait costs
-    // about as much issue time as four M=128, N=32 MMAs).
+    // (the dequantizers' stores and the MMA's reads). A TMEM_A stage holds KPS = 4 k-blocks (one
+    // raw super-block, decoded by one dequantizer group; the groups alternate stages) and one
+    // barrier pair serves the activations and the weights of the stage, so the MMA issuer and the
+    // dequantizers wait once per four k-blocks (an mbarrier wait costs about as much issue time as
+    // four M=128, N=32 MMAs).
     static constexpr bool TMEM_A = FMT != FMT_F16 && !PAIR && BT <= 128;
-#ifndef JK_KPS
     static constexpr int KPS = TMEM_A ? 4 : 1;                  // k-blocks per stage
-#else
-    static constexpr int KPS = TMEM_A ? JK_KPS : 1;
-#endif
     static constexpr int B_ATOM = (PAIR ? BT / 2 : BT) * 128;  // one k-block of activations (a pair CTA: half the rows)
     static constexpr int B_STAGE = KPS * B_ATOM;
     static constexpr int raw_bytes = RawTile<FMT>::bytes;
@@ -661,17 +658,18 @@ __device__ __forceinline__ void dequant_role(const Sched& sched, SegState& ss, u
     }
 }
 
-// Dequantizer role with tensor-memory A stages (Smem::TMEM_A): group g decodes the k-blocks
-// kb with kb % 2 == g into TMEM lanes of its rows (one tcgen05.st of 32 columns per k-block);
-// both groups wait for a stage to be free and arrive on its full barrier once per stage, whether
-// or not the stage holds a k-block of theirs (a segment's edge stages may hold one k-block).
+// Dequantizer role with tensor-memory A stages (Smem::TMEM_A). A stage is one raw super-block
+// (KPS = 4 k-blocks, the stage and raw-ring counters advance together) and the two groups take
+// alternate stages: group g decodes the whole stage st with st % 2 == g (one super-block header
+// decode, one raw wait and one empty wait per 4 k-blocks per group) into TMEM lanes of its rows,
+// one tcgen05.st of 32 columns per k-block, then arrives once on the stage's full barrier.
 template <int FMT, bool BF16, int BT>
 __device__ __forceinline__ void dequant_role_tmem(const Sched& sched, SegState& ss, uint8_t* smem, int row_in_tile,
                                                   int grp, const WView& w, uint32_t* err, bool& ok, uint32_t bar0,
                                                   int lane, uint32_t tmem) {
     using L = Smem<FMT, BT, false>;
     constexpr int S = L::SX, R = L::R, KPS = L::KPS;
-    static_assert(KPS % 2 == 0, "the two dequantizer groups alternate k-blocks within a stage");
+    static_assert(KPS == 4, "a stage is one raw super-block");
     auto full = [&](int st) { return bar0 + 8u * (L::bar_full_b + st); };
     auto empty = [&](int st) { return bar0 + 8u * (L::bar_empty_b + st); };
     auto raw_full = [&](int r) { return bar0 + 8u * (L::bar_raw_full + r); };
@@ -679,58 +677,53 @@ __device__ __forceinline__ void dequant_role_tmem(const Sched& sched, SegState& 
     const int sw = row_in_tile & 7;
     const uint32_t tlanes = tmem + ((uint32_t)(row_in_tile & ~31) << 16) + L::TMEM_A0;
     SbDequant<FMT, BF16> dq;
-    int st = 0, raw_n = 0;
+    int st = 0;  // stage = raw super-block counter
     Seg sg;
     while (ok && seg_next(sched, ss, sg)) {
         const int64_t row = tile_at<BW, BT>(sched, sg.tile, 0, 0).wrow0 + row_in_tile;
         const bool row_ok = row < w.rows;
         const int64_t rr = row_ok ? row : 0;
         const int sb_lo = sg.kb_lo >> 2, sb_hi = (sg.kb_hi - 1) >> 2;
-        dq.prefetch(w, rr, sb_lo);
-        for (int sb = sb_lo; sb <= sb_hi && ok; ++sb) {
-            const int r = raw_n++;
-            const int slot = r % R;
-            ok = __all_sync(0xFFFFFFFFu, mbar_wait(raw_full(slot), (r / R) & 1, err));
+        const int first_own = sb_lo + (((st & 1) == grp) ? 0 : 1);
+        if (first_own <= sb_hi) dq.prefetch(w, rr, first_own);
+        for (int sb = sb_lo; sb <= sb_hi && ok; ++sb, ++st) {
+            if ((st & 1) != grp) continue;
+            const int s = st % S, slot = st % R;
+            ok = __all_sync(0xFFFFFFFFu, mbar_wait(raw_full(slot), (st / R) & 1, err));
             if (!ok) break;
-            JK_TRACE_POINT(10, r);
+            JK_TRACE_POINT(10, st);
             const uint8_t* raw_row = smem + L::off_raw + slot * L::raw_bytes +
                                      row_in_tile * (FMT == FMT_Q4K ? 144 : FMT == FMT_Q6K ? 208 : 128);
             dq.begin(raw_row, w, rr, row_ok, sb);
-            if (sb < sb_hi) dq.prefetch(w, rr, sb + 1);
-            JK_TRACE_POINT(11, r);
+            if (sb + 2 <= sb_hi) dq.prefetch(w, rr, sb + 2);
+            JK_TRACE_POINT(11, st);
+            if (st >= S) ok = __all_sync(0xFFFFFFFFu, mbar_wait(empty(s), ((st / S) - 1) & 1, err));
+            if (!ok) break;
+            JK_TRACE_POINT(6, st);
+            tc_fence_after();  // the MMAs that read the stage before have completed
+            const int kb_lo = 4 * sb > sg.kb_lo ? 4 * sb : sg.kb_lo;
+            const int kb_hi = 4 * sb + 4 < sg.kb_hi ? 4 * sb + 4 : sg.kb_hi;
 #pragma unroll
             for (int j = 0; j < 4; ++j) {
                 const int kb = 4 * sb + j;
-                if (kb < sg.kb_lo || kb >= sg.kb_hi) continue;
-                const int s = st % S;
-                if (kb == sg.kb_lo || kb % KPS == 0) {  // the stage's first k-block: wait until it is free
-                    if (st >= S) ok = __all_sync(0xFFFFFFFFu, mbar_wait(empty(s), ((st / S) - 1) & 1, err));
-                    if (!ok) break;
-                    JK_TRACE_POINT(6, st);
-                    tc_fence_after();  // the MMAs that read the stage before have completed
+                if (kb < kb_lo || kb >= kb_hi) continue;
+                RegRow o;
+                switch (j) {
+                case 0: dq.template kblock<0, 0>(raw_row, row_in_tile, sw, o); dq.template kblock<0, 1>(raw_row, row_in_tile, sw, o); break;
+                case 1: dq.template kblock<1, 0>(raw_row, row_in_tile, sw, o); dq.template kblock<1, 1>(raw_row, row_in_tile, sw, o); break;
+                case 2: dq.template kblock<2, 0>(raw_row, row_in_tile, sw, o); dq.template kblock<2, 1>(raw_row, row_in_tile, sw, o); break;
+                default: dq.template kblock<3, 0>(raw_row, row_in_tile, sw, o); dq.template kblock<3, 1>(raw_row, row_in_tile, sw, o); break;
                 }
-                if ((kb & 1) == grp) {
-                    RegRow o;
-                    switch (j) {
-                    case 0: dq.template kblock<0, 0>(raw_row, row_in_tile, sw, o); dq.template kblock<0, 1>(raw_row, row_in_tile, sw, o); break;
-                    case 1: dq.template kblock<1, 0>(raw_row, row_in_tile, sw, o); dq.template kblock<1, 1>(raw_row, row_in_tile, sw, o); break;
-                    case 2: dq.template kblock<2, 0>(raw_row, row_in_tile, sw, o); dq.template kblock<2, 1>(raw_row, row_in_tile, sw, o); break;
-                    default: dq.template kblock<3, 0>(raw_row, row_in_tile, sw, o); dq.template kblock<3, 1>(raw_row, row_in_tile, sw, o); break;
-                    }
-                    tmem_st32(tlanes + (uint32_t)(32 * (KPS * s + kb % KPS)), o.w);
-                }
-                if (kb == sg.kb_hi - 1 || kb % KPS == KPS - 1) {  // the stage's last k-block: publish it
-                    tmem_st_wait();
-                    tc_fence_before();
-                    __syncwarp();
-                    JK_TRACE_POINT(9, st);
-                    if (lane == 0) mbar_arrive(full(s));
-                    ++st;
-                }
+                tmem_st32(tlanes + (uint32_t)(32 * (KPS * s + j)), o.w);
             }
-            if (!ok) break;
+            tmem_st_wait();
+            tc_fence_before();
             __syncwarp();
-            if (lane == 0) mbar_arrive(raw_empty(slot));
+            JK_TRACE_POINT(9, st);
+            if (lane == 0) {
+                mbar_arrive(full(s));
+                mbar_arrive(raw_empty(slot));
+            }
         }
     }
 }
@@ -778,8 +771,9 @@ gemm_tc_kernel(const __grid_constant__ CUtensorMap tm_x, const __grid_constant__
 
     if (threadIdx.x == 0) {
         for (int s = 0; s < SX; ++s) {
-            // TMEM_A: the stage's producer arrival (with its bytes) and every dequantizer warp
-            mbar_init(full_b(s), L::TMEM_A ? 1 + DQ_WARPS : 1);
+            // TMEM_A: the stage's producer arrival (with its bytes) and the warps of the
+            // dequantizer group that decodes the stage
+            mbar_init(full_b(s), L::TMEM_A ? 1 + DQ_WARPS / 2 : 1);
             mbar_init(empty_b(s), 1);
         }
         for (int s = 0; s < SA; ++s) {
@@ -789,7 +783,9 @@ gemm_tc_kernel(const __grid_constant__ CUtensorMap tm_x, const __grid_constant__
         }
         for (int r = 0; r < R; ++r) {
             mbar_init(raw_full(r), 1);
-            mbar_init(raw_empty(r), DQ_WARPS);
+            // every dequantizer warp reads each raw super-block, except with TMEM_A stages, where
+            // one group decodes it
+            mbar_init(raw_empty(r), L::TMEM_A ? DQ_WARPS / 2 : DQ_WARPS);
         }
         for (int b = 0; b < 2; ++b) {
             mbar_init(acc_full(b), 1);

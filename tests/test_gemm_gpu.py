@@ -107,9 +107,13 @@ def test_multi_expert_matrix_dense_product_uses_expert_zero(gpu):
 def test_heuristic_plans_and_matmul(gpu):
     from jevons_kernels.gemm import Buf, Plan, SplitScratch, matmul
     w, _, dense = make_weights(gpu, KINDS["Q4_K"], 10240, 2560, seed=1)
-    for m, want in ((1, 0), (2, 0), (32, 32), (256, 256)):
+    # row tiles stop at 128 for block-quantized weights (tensor-memory weight stages)
+    for m, want in ((1, 0), (2, 0), (32, 32), (100, 128), (256, 128)):
         p = Plan.heuristic(w, m, False)
         assert p.bm == want and p.valid_for(w, m)
+    # 80 x 2 tiles of m=256 on this device's SMs leave most of a second wave idle: stream-K
+    assert Plan.heuristic(w, 256, False, 148).splits > 1
+    assert Plan.heuristic(w, 256, False, 160).splits == 1
         assert Plan.heuristic(w, m, True).splits == 1 and Plan.heuristic(w, m, True).bm > 0
     x, x_exact = activations(32, 2560, torch.bfloat16, seed=1)
     out = torch.empty(32, 10240, device="cuda")

@@ -55,10 +55,12 @@ constexpr int A_STAGE_BYTES = BW * KB * 2;
 //
 // When the dequantized weights go to tensor memory instead (TMEM_A below), a warp may only write
 // the TMEM lanes of its own sub-partition (lanes 32 (w % 4) ..), so dequantizer slot s (rows
-// 32 (s % 4) ..) must sit on a warp with w % 4 == s % 4; the MMA issuer then shares its
-// sub-partition with two dequantizers:
-//   w: 0 producer | 1 MMA | 4..7 epilogue | 10 raw producer | 15 idle
-//      dequantizers 8, 9, 2, 3 (group 0) and 12, 13, 14, 11 (group 1)
+// 32 (s % 4) ..) sits on warp 8 + s; such CTAs have 20 warps and three dequantizer groups (the
+// decoding, not the MMA, bounds their main loop):
+//   w: 0 producer | 1 MMA | 2 raw producer | 3 idle | 4..7 epilogue
+//      dequantizers 8..11 (group 0), 12..15 (group 1), 16..19 (group 2)
+// (with 128-row activation tiles only two tensor-memory stages fit, and such CTAs keep 16 warps
+// and two groups: see Smem::DQ_GROUPS)
 // k-blocks per MMA-issue batch (one round of barrier waits and commits per batch)
 #ifndef JK_MMA_BATCH
 constexpr int MMA_BATCH = 1;
@@ -66,27 +68,19 @@ constexpr int MMA_BATCH = 1;
 constexpr int MMA_BATCH = JK_MMA_BATCH;
 #endif
 constexpr int PRODUCER_WARP = 0, MMA_WARP = 1, EPI_WARP0 = 4, EPI_WARPS = 4, DQ_WARPS = 8;
-constexpr int THREADS = 512;
 constexpr int EPI_THREADS = 32 * EPI_WARPS;  // 128: 1 per weight row
 template <bool TMEM_A>
-constexpr int RAW_WARP = TMEM_A ? 10 : 9;
+constexpr int RAW_WARP = TMEM_A ? 2 : 9;
 template <bool TMEM_A>
 __device__ __forceinline__ int dq_slot(int warp) {  // position among the dequantizer warps, or -1
-    // nibble w: slot, F = not a dequantizer
-    constexpr unsigned long long tbl = TMEM_A ? 0xF6547F10FFFF32FFull : 0x76F543F2FFFF10FFull;
-    const int v = (int)((tbl >> (4 * warp)) & 15u);
-    return v == 15 ? -1 : v;
-}
-
-// The tensor-memory table keeps every dequantizer slot on a warp of its TMEM lane quarter.
-constexpr bool tmem_slots_ok() {
-    for (int w = 0; w < 16; ++w) {
-        const int v = (int)((0xF6547F10FFFF32FFull >> (4 * w)) & 15u);
-        if (v != 15 && (v & 3) != (w & 3)) return false;
+    if constexpr (TMEM_A) {
+        return warp >= 8 ? warp - 8 : -1;  // slot s on warp 8 + s: (8 + s) % 4 == s % 4
+    } else {
+        constexpr unsigned long long tbl = 0x76F543F2FFFF10FFull;  // nibble w: slot, F = none
+        const int v = (int)((tbl >> (4 * warp)) & 15u);
+        return v == 15 ? -1 : v;
     }
-    return true;
 }
-static_assert(tmem_slots_ok(), "dequantizer slot outside its warp's TMEM lanes");
 
 template <int FMT>
 struct RawTile {
@@ -150,6 +144,13 @@ struct Smem {
     static constexpr Rings rings = TMEM_A ? pick_rings_tmem(B_STAGE, raw_bytes, (512 - 2 * BT) / (32 * KPS))
                                           : pick_rings(B_STAGE, raw_bytes);
     static constexpr int SX = rings.sx, SA = rings.sa, R = rings.r;
+    // Groups of 4 dequantizer warps. A TMEM_A group waits on a stage's empty barrier by phase
+    // parity, which is only sound if no group can reach a stage while the stage S places earlier
+    // is still unconsumed: group g fills stage st after its own stage st - G, whose stage was
+    // freed by the MMAs of stage st - G - S, so G <= S keeps every waiter within one phase.
+    static constexpr int DQ_GROUPS = TMEM_A ? (SA < 3 ? SA : 3) : 2;
+    static constexpr int THREADS = TMEM_A ? 32 * (8 + 4 * DQ_GROUPS) : 512;
+    static_assert(!TMEM_A || (DQ_GROUPS >= 2 && DQ_GROUPS <= SA), "dequantizer groups vs stages");
     static_assert(FMT != FMT_F16 || SX == SA, "FP16 weights share the activation ring");
     static constexpr uint32_t TMEM_COLS = TMEM_A ? 512 : 2 * BT;
     static_assert(!TMEM_A || (SX == SA && TMEM_A0 + 32 * KPS * SA <= TMEM_COLS), "tensor memory budget");
@@ -659,10 +660,10 @@ __device__ __forceinline__ void dequant_role(const Sched& sched, SegState& ss, u
 }
 
 // Dequantizer role with tensor-memory A stages (Smem::TMEM_A). A stage is one raw super-block
-// (KPS = 4 k-blocks, the stage and raw-ring counters advance together) and the two groups take
-// alternate stages: group g decodes the whole stage st with st % 2 == g (one super-block header
-// decode, one raw wait and one empty wait per 4 k-blocks per group) into TMEM lanes of its rows,
-// one tcgen05.st of 32 columns per k-block, then arrives once on the stage's full barrier.
+// (KPS = 4 k-blocks, the stage and raw-ring counters advance together) and the G groups take
+// turns: group g decodes the whole stage st with st % G == g (one super-block header decode, one
+// raw wait and one empty wait per 4 k-blocks per group) into TMEM lanes of its rows, one
+// tcgen05.st of 32 columns per k-block, then arrives once on the stage's full barrier.
 template <int FMT, bool BF16, int BT>
 __device__ __forceinline__ void dequant_role_tmem(const Sched& sched, SegState& ss, uint8_t* smem, int row_in_tile,
                                                   int grp, const WView& w, uint32_t* err, bool& ok, uint32_t bar0,
@@ -670,6 +671,7 @@ __device__ __forceinline__ void dequant_role_tmem(const Sched& sched, SegState& 
     using L = Smem<FMT, BT, false>;
     constexpr int S = L::SX, R = L::R, KPS = L::KPS;
     static_assert(KPS == 4, "a stage is one raw super-block");
+    constexpr int G = L::DQ_GROUPS;
     auto full = [&](int st) { return bar0 + 8u * (L::bar_full_b + st); };
     auto empty = [&](int st) { return bar0 + 8u * (L::bar_empty_b + st); };
     auto raw_full = [&](int r) { return bar0 + 8u * (L::bar_raw_full + r); };
@@ -684,10 +686,10 @@ __device__ __forceinline__ void dequant_role_tmem(const Sched& sched, SegState& 
         const bool row_ok = row < w.rows;
         const int64_t rr = row_ok ? row : 0;
         const int sb_lo = sg.kb_lo >> 2, sb_hi = (sg.kb_hi - 1) >> 2;
-        const int first_own = sb_lo + (((st & 1) == grp) ? 0 : 1);
+        const int first_own = sb_lo + (grp - st % G + G) % G;
         if (first_own <= sb_hi) dq.prefetch(w, rr, first_own);
         for (int sb = sb_lo; sb <= sb_hi && ok; ++sb, ++st) {
-            if ((st & 1) != grp) continue;
+            if (st % G != grp) continue;
             const int s = st % S, slot = st % R;
             ok = __all_sync(0xFFFFFFFFu, mbar_wait(raw_full(slot), (st / R) & 1, err));
             if (!ok) break;
@@ -695,7 +697,7 @@ __device__ __forceinline__ void dequant_role_tmem(const Sched& sched, SegState& 
             const uint8_t* raw_row = smem + L::off_raw + slot * L::raw_bytes +
                                      row_in_tile * (FMT == FMT_Q4K ? 144 : FMT == FMT_Q6K ? 208 : 128);
             dq.begin(raw_row, w, rr, row_ok, sb);
-            if (sb + 2 <= sb_hi) dq.prefetch(w, rr, sb + 2);
+            if (sb + G <= sb_hi) dq.prefetch(w, rr, sb + G);
             JK_TRACE_POINT(11, st);
             if (st >= S) ok = __all_sync(0xFFFFFFFFu, mbar_wait(empty(s), ((st / S) - 1) & 1, err));
             if (!ok) break;
@@ -734,7 +736,7 @@ __device__ __forceinline__ void dequant_role_tmem(const Sched& sched, SegState& 
 // 128-row accumulator; completions are committed to both CTAs. Halving the activation bytes each
 // SM loads per k-block is the point: at BT=256 those tiles, not the MMAs, bound the main loop.
 template <int FMT, bool BF16, int BT, bool PAIR>
-__global__ void __launch_bounds__(THREADS, 1)
+__global__ void __launch_bounds__(Smem<FMT, BT, PAIR>::THREADS, 1)
 gemm_tc_kernel(const __grid_constant__ CUtensorMap tm_x, const __grid_constant__ CUtensorMap tm_w, WView w,
                float* __restrict__ out, int64_t m, int64_t ldo, Sched sched, float* __restrict__ ws_part,
                uint32_t* __restrict__ ws_flag, uint32_t* err) {
@@ -773,7 +775,7 @@ gemm_tc_kernel(const __grid_constant__ CUtensorMap tm_x, const __grid_constant__
         for (int s = 0; s < SX; ++s) {
             // TMEM_A: the stage's producer arrival (with its bytes) and the warps of the
             // dequantizer group that decodes the stage
-            mbar_init(full_b(s), L::TMEM_A ? 1 + DQ_WARPS / 2 : 1);
+            mbar_init(full_b(s), L::TMEM_A ? 1 + 4 : 1);
             mbar_init(empty_b(s), 1);
         }
         for (int s = 0; s < SA; ++s) {
@@ -785,7 +787,7 @@ gemm_tc_kernel(const __grid_constant__ CUtensorMap tm_x, const __grid_constant__
             mbar_init(raw_full(r), 1);
             // every dequantizer warp reads each raw super-block, except with TMEM_A stages, where
             // one group decodes it
-            mbar_init(raw_empty(r), L::TMEM_A ? DQ_WARPS / 2 : DQ_WARPS);
+            mbar_init(raw_empty(r), L::TMEM_A ? 4 : DQ_WARPS);
         }
         for (int b = 0; b < 2; ++b) {
             mbar_init(acc_full(b), 1);
@@ -1250,12 +1252,12 @@ gemm_tc_kernel(const __grid_constant__ CUtensorMap tm_x, const __grid_constant__
 // Shared-memory opt-in and CTAs per SM, once per (kernel instantiation, device): `cache` must be
 // a static of the instantiation's own launcher (all instantiations share one function type).
 template <class K>
-int prepare_kernel(K kern, int smem, int device, int (&cache)[64]) {
+int prepare_kernel(K kern, int smem, int threads, int device, int (&cache)[64]) {
     if (device < 0 || device >= 64) return -1;
     if (cache[device] == 0) {
         if (cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, smem) != cudaSuccess) return -1;
         int per_sm = 0;
-        if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, kern, THREADS, smem) != cudaSuccess || per_sm < 1)
+        if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, kern, threads, smem) != cudaSuccess || per_sm < 1)
             return -1;
         cache[device] = per_sm;
     }
@@ -1289,7 +1291,7 @@ jk_status launch_tc(const LaunchArgs& a) {
     int dev = 0;
     cudaGetDevice(&dev);
     static int per_sm_cache[64] = {};
-    const int per_sm = prepare_kernel(kern, L::total, dev, per_sm_cache);
+    const int per_sm = prepare_kernel(kern, L::total, L::THREADS, dev, per_sm_cache);
     if (per_sm < 0) return cuda_fail(cudaGetLastError(), "gemm kernel attributes");
     const WView& w = a.wq->view;
     Sched s{};
@@ -1310,7 +1312,7 @@ jk_status launch_tc(const LaunchArgs& a) {
     const int64_t work = s.sk ? s.tiles * s.kbt : s.tiles;
     if constexpr (PAIR) {
         cudaLaunchConfig_t cfg = {};
-        cfg.blockDim = dim3(THREADS);
+        cfg.blockDim = dim3(L::THREADS);
         cfg.dynamicSmemBytes = L::total;
         cfg.stream = a.stream;
         cudaLaunchAttribute attr[1];
@@ -1348,7 +1350,7 @@ jk_status launch_tc(const LaunchArgs& a) {
         if (a.grid_cap > 0 && g > a.grid_cap) g = a.grid_cap;
         if (g > work) g = work;
         s.G = (int)g;
-        kern<<<s.G, THREADS, L::total, a.stream>>>(*a.tm_x, a.wq->tm_w, w, a.out, a.m, a.ldo, s, a.ws_part,
+        kern<<<s.G, L::THREADS, L::total, a.stream>>>(*a.tm_x, a.wq->tm_w, w, a.out, a.m, a.ldo, s, a.ws_part,
                                                    a.ws_flag, device_error_word(a.wq->device));
         return cuda_fail(cudaGetLastError(), "gemm launch");
     }

@@ -250,6 +250,25 @@ def test_stream_k_fixup_shapes(gpu, name, n, k, m, bn):
     assert gpu.device_error() == 0
 
 
+@pytest.mark.parametrize("name", ["Q4_K", "Q6_K", "Q8_0", "Q5_0"])
+def test_long_k_wraps_every_stage_ring(gpu, name):
+    """k = 10240 (160 k-blocks) wraps the weight-stage rings many times for every row tile, with
+    whole tiles and with stream-K: the tensor-memory stage rings of 32..128-row tiles hold only
+    2 or 3 stages, so any phase-tracking slip between the dequantizer groups shows up here."""
+    from jevons_kernels.gemm import Buf, Plan, SplitScratch, matmul_plan
+    n, k, m = 256, 10240, 200
+    w, _, dense = make_weights(gpu, KINDS[name], n, k, seed=31)
+    x, x_exact = activations(m, k, torch.bfloat16, seed=32, sigma=0.5)
+    want = oracle.matmul_f64(x_exact, dense)
+    scratch = SplitScratch(gpu)
+    for bm in (32, 64, 128, 256):
+        for splits in (1, 2):
+            out = torch.full((m, n), float("nan"), device="cuda")
+            matmul_plan(gpu, Buf(x), m, w, Buf(out), None, scratch, Plan(bm, 128, splits))
+            assert_close(f"{name} k={k} bm={bm} s={splits}", out.cpu().numpy(), x_exact, dense, want)
+    assert gpu.device_error() == 0
+
+
 def test_sm_cap_keeps_products_correct(gpu):
     """jk_set_max_ctas: products launched under a cap (stream-K, whole tiles, small-row kernel)
     stay within tolerance; the cap is per device and 0 lifts it."""

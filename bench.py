@@ -459,7 +459,7 @@ def run_ours(args):
                        "activations": "bf16 N(0,1)"},
             "roofline": {"bound": "tensor", "achieved": achieved, "peak": peak, "unit": "TFLOP/s",
                          "frac": achieved / peak, "traffic": traffic,
-                         "kernel": "gemm_tc_kernel<Q4_K,bf16,256>",
+                         "kernel": f"gemm_tc_kernel<Q4_K,bf16,{plan.bm}>",
                          "per_launch_ms": per_launch_ms,
                          "peak_source": f"{pk_kind} bf16_tflops_sustained (kernel timed inside a long step)"},
             "gemv": {"metric": "Q4_K GEMV weight-GB/s (M=1)", "value": gemv_gbs, "unit": "GB/s",

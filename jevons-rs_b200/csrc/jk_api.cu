@@ -682,8 +682,10 @@ jk::WView dense_view(const jk_qmatrix* w) {
 // Plan::heuristic (gemm.rs:989-1004), adapted to this kernel: the activation-row tile grows with
 // m but stops at 128 for block-quantized weights (there the dequantized weights live in tensor
 // memory next to two 128-column accumulators, which measures faster than 256-row tiles with
-// shared-memory weight stages); split-K (`splits > 1`, the stream-K schedule) is chosen when whole
-// tiles would leave more than a quarter of the last wave's SMs idle.
+// shared-memory weight stages); split-K (`splits > 1`, the stream-K schedule) is chosen only when
+// whole tiles would leave more than half of the SMs without a tile: measured on B200, whole tiles
+// win whenever there are about as many tiles as SMs or more (the stream-K fix-up costs more than an
+// uneven last wave), while few long tiles (e.g. N=2560, K=10240) need K split across SMs.
 extern "C" jk_status jk_plan_heuristic(const jk_qmatrix* w, size_t m, int row_invariant, int sms, jk_plan* out) {
     if (!w || !out) return fail(JK_ERR_INVALID, "null pointer");
     int bm = row_tile_for(m);
@@ -699,9 +701,8 @@ extern "C" jk_status jk_plan_heuristic(const jk_qmatrix* w, size_t m, int row_in
     }
     const size_t target = sms > 0 ? (size_t)sms : (size_t)jk::sm_count(w->device);
     const size_t tiles = (w->n + 127) / 128 * ((m + bm - 1) / bm);
-    const size_t waves = (tiles + target - 1) / target;
-    const bool balanced = tiles * 4 >= waves * target * 3;
-    *out = {bm, bn, balanced || w->k / 64 < 2 ? 1 : 2};
+    const bool enough_tiles = tiles * 2 >= target;
+    *out = {bm, bn, enough_tiles || w->k / 64 < 8 ? 1 : 2};
     return JK_OK;
 }
 

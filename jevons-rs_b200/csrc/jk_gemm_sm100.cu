@@ -1087,6 +1087,10 @@ gemm_tc_kernel(const __grid_constant__ CUtensorMap tm_x, const __grid_constant__
                 // per-thread loads, so a whole ring of them is in flight at once.
                 const int nc = u_last - unit;
                 const bool bulk_fix = owner && nc > 0 && ss.next >= ss.end;
+                // The CTA's last tile: the pipeline's shared memory is idle, so the output rows are
+                // staged there and written whole with bulk stores (per-element column stores of a
+                // 128 x 128 f32 tile took ~6 us on the exposed tail of a product, bulk rows ~2x less).
+                const bool staged = !contributor && vec_out && !sched.jobs && ss.next >= ss.end;
                 const int nchunks = bulk_fix ? (BT / CH) * nc : 0;
                 auto issue_chunk = [&](int q) {
                     const int r = q / nc, ci = q - r * nc;
@@ -1149,7 +1153,7 @@ gemm_tc_kernel(const __grid_constant__ CUtensorMap tm_x, const __grid_constant__
                             }
                         }
                         JK_TRACE_POINT(13, c0 / CH);
-                        if (bulk_fix && vec_out) {
+                        if (staged) {
                             // stage the round as [row of out][BW] and write whole rows with bulk
                             // stores; the two staging buffers alternate between rounds
                             float* tp = reinterpret_cast<float*>(smem + L::off_fix_out + ((c0 / CH) & 1) * L::FIX_CHUNK);
@@ -1200,6 +1204,7 @@ gemm_tc_kernel(const __grid_constant__ CUtensorMap tm_x, const __grid_constant__
                     }
                     fix_q += nchunks;
                 }
+                if (staged && !bulk_fix && lane == 0) bulk_wait_all();  // smem read before the CTA exits
                 JK_TRACE_POINT(11, seg_i);
                 if (contributor) {
                     // every partial store of the tile precedes the barrier; one gpu-scope fence by

@@ -263,13 +263,17 @@ __global__ void __launch_bounds__(THREADS, MR <= 2 ? 2 : 1) gemv_kernel(WView w,
     const int per_iter = WARPS / P;
     const int st_lo = (int)part * geo.steps / P, st_hi = (int)(part + 1) * geo.steps / P;
     const int nseg = (int)((st_hi - st_lo + geo.KS - 1) / geo.KS);
-    const int first = (int)blockIdx.x * per_iter + grp;
+    // Row groups are dealt to the CTAs round-robin: the j-th row group of this CTA is
+    // blockIdx.x + j * gridDim.x, j = kk * per_iter + grp for iteration kk of warp group grp. Every
+    // SM then holds the same number of row groups to within one whatever the grid (dealing blocks
+    // of per_iter consecutive row groups left some SMs with twice the average).
+    const int n_c = (int)blockIdx.x < geo.rowgroups ? (geo.rowgroups - 1 - (int)blockIdx.x) / (int)gridDim.x + 1 : 0;
+    const int first = (int)blockIdx.x + grp * (int)gridDim.x;
     const int stride = (int)gridDim.x * per_iter;
-    const int kg = first < geo.rowgroups ? (geo.rowgroups - 1 - first) / stride + 1 : 0;
+    const int kg = grp < n_c ? (n_c - 1 - grp) / per_iter + 1 : 0;
     const int items = kg * nseg;
     // all warps of the CTA run the same number of row-group iterations (group barriers)
-    const int k_cta = ((int)blockIdx.x * per_iter < geo.rowgroups)
-                              ? (geo.rowgroups - 1 - (int)blockIdx.x * per_iter) / stride + 1 : 0;
+    const int k_cta = (n_c + per_iter - 1) / per_iter;
 
     const uint32_t bar0 = smem_u32(&bars[warp * SLOTS_PER_WARP]);
     const uint32_t slot0 = smem_u32(slots) + (uint32_t)(warp * SLOTS_PER_WARP) * (uint32_t)geo.slot_bytes;
@@ -645,7 +649,9 @@ jk_status launch_gemv_t(const WView& w, const void* x, int x_dtype, int mrows, f
     cudaError_t e = cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, kern, THREADS, smem);
     if (e != cudaSuccess) return cuda_fail(e, "gemv occupancy");
     if (per_sm < 1) return fail(JK_ERR_UNSUPPORTED, "gemv: kernel does not fit on an SM");
-    const int64_t want = ((int64_t)geo.rowgroups * geo.P + WARPS - 1) / WARPS;
+    // every CTA that can be resident (row groups are dealt round-robin, so a full grid balances
+    // the SMs), but no more CTAs than row groups
+    const int64_t want = (int64_t)geo.rowgroups;
     // grouped: the live jobs share the SMs
     const int64_t cap = ((int64_t)per_sm * sms + jobs_est - 1) / jobs_est;
     const unsigned grid = (unsigned)(want < cap ? want : cap);

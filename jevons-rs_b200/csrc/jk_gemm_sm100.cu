@@ -163,7 +163,7 @@ struct Smem {
     // (bulk-copied, FIX_CH activation rows x BW f32 each, contiguous in the workspace), then two
     // output staging buffers of the same size from which whole 512-byte output rows are written
     // by bulk stores.
-    static constexpr int FIX_CH = BT < 64 ? BT : 64;
+    static constexpr int FIX_CH = BT < 32 ? BT : 32;
     static constexpr int FIX_CHUNK = FIX_CH * BW * 4;
     static constexpr int FIX_NB = off_bar / FIX_CHUNK - 2 < 16 ? off_bar / FIX_CHUNK - 2 : 16;
     static constexpr int off_fix_out = FIX_NB * FIX_CHUNK;
@@ -223,6 +223,13 @@ __device__ __forceinline__ TileAt tile_at(const Sched& s, int64_t tile, int rank
     }
     return t;
 }
+
+// Programmatic dependent launch (the launch sets cudaLaunchAttributeProgrammaticStreamSerialization):
+// gdc_launch lets the next kernel on the stream start on SMs this grid frees; gdc_wait blocks until
+// the previous kernel on the stream has completed and its memory is visible (a no-op without the
+// attribute).
+__device__ __forceinline__ void gdc_launch() { asm volatile("griddepcontrol.launch_dependents;" ::: "memory"); }
+__device__ __forceinline__ void gdc_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
 
 struct Seg {
     int64_t tile;
@@ -811,6 +818,13 @@ gemm_tc_kernel(const __grid_constant__ CUtensorMap tm_x, const __grid_constant__
     tc_fence_after();
     const uint32_t tmem = *tmem_holder;
     JK_TRACE_POINT(14, 0);
+    // The next product may start on the SMs this grid frees and fill its pipeline (raw weights,
+    // dequantized stages) while this grid's last tiles finish. Everything that reads what the
+    // previous kernel on the stream wrote -- the activations (the producer), the grouped job table
+    // (every role), the stream-K flags and partials (epilogues, after their MMAs and so after the
+    // producer) -- waits for it first; weights are read-only for the whole product.
+    gdc_launch();
+    if (sched.jobs) gdc_wait();
 
     bool ok = true;
     SegState ss;
@@ -823,6 +837,7 @@ gemm_tc_kernel(const __grid_constant__ CUtensorMap tm_x, const __grid_constant__
     const bool leader = lane == 0;
     if (warp == PRODUCER_WARP) {
         // --------------------- activation (and FP16 weight) producer ---------------------
+        gdc_wait();  // the activations may come from the previous kernel
         if (leader) {
             tma_prefetch(&tm_x);
             tma_prefetch(&tm_w);
@@ -1355,8 +1370,19 @@ jk_status launch_tc(const LaunchArgs& a) {
         if (a.grid_cap > 0 && g > a.grid_cap) g = a.grid_cap;
         if (g > work) g = work;
         s.G = (int)g;
-        kern<<<s.G, L::THREADS, L::total, a.stream>>>(*a.tm_x, a.wq->tm_w, w, a.out, a.m, a.ldo, s, a.ws_part,
-                                                   a.ws_flag, device_error_word(a.wq->device));
+        cudaLaunchConfig_t cfg = {};
+        cfg.gridDim = dim3((unsigned)s.G);
+        cfg.blockDim = dim3(L::THREADS);
+        cfg.dynamicSmemBytes = L::total;
+        cfg.stream = a.stream;
+        cudaLaunchAttribute attr[1];
+        attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+        attr[0].val.programmaticStreamSerializationAllowed = 1;
+        cfg.attrs = attr;
+        cfg.numAttrs = 1;
+        cudaError_t e = cudaLaunchKernelEx(&cfg, kern, *a.tm_x, a.wq->tm_w, w, a.out, a.m, a.ldo, s, a.ws_part,
+                                           a.ws_flag, device_error_word(a.wq->device));
+        if (e != cudaSuccess) return cuda_fail(e, "gemm launch");
         return cuda_fail(cudaGetLastError(), "gemm launch");
     }
 }

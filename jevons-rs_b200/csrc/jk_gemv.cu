@@ -6,10 +6,9 @@
 // K segment. Lanes 0..7 copy the group's 8 row segments (and their f16 scales / high-bit words)
 // from HBM into a shared-memory slot with one bulk async copy each (cp.async.bulk, completion on
 // the slot's mbarrier). Every warp owns two slots, so two items per warp, 16 per CTA, are in
-// flight. The first two are issued at the very top of the kernel, before the kernel waits on the
-// previous grid (programmatic dependent launch) and before the activations are staged. A CTA
-// therefore has ~90 KB of weights in flight from its first instruction, which is the whole
-// per-SM share of a decode-sized matrix. The launch asks for 2 CTAs per SM, so the next product's
+// flight. The first is issued at the very top of the kernel, before the kernel waits on the
+// previous grid (programmatic dependent launch); the second right after the activations are
+// staged, so the activation loads do not queue behind it. The launch asks for 2 CTAs per SM, so the next product's
 // CTAs start streaming while this one finishes.
 //
 // Work split. `P` warps (1, 2, 4 or 8) share a row group, each taking a contiguous 1/P of its K
@@ -326,12 +325,14 @@ __global__ void __launch_bounds__(THREADS, MR <= 2 ? 2 : 1) gemv_kernel(WView w,
     };
 
     if (items > 0) issue(0);
-    if (items > 1) issue(1);
     JK_TRACE_POINT(2, 0);
 
     pdl_wait();  // activations come from the previous grid; outputs may be read by it
     JK_TRACE_POINT(3, 0);
     stage_x<FMT, MR>(geo, x, x_dtype, mrows, xs, src);
+    // the second item's copies go out after the activations are read: issued before, they queued
+    // ahead of the activation loads (measured 6.9 -> 6.5 us per 14.7 MB product)
+    if (items > 1) issue(1);
     __syncthreads();
     JK_TRACE_POINT(4, 0);
 

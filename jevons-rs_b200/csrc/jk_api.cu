@@ -358,7 +358,7 @@ extern "C" jk_status jk_gpu_init(int device) {
     e = cudaGetDeviceProperties(&p, device);
     if (e != cudaSuccess) return cuda_fail(e, "cudaGetDeviceProperties");
     if (p.major != 10) {
-        char buf[160];
+        char buf[400];  // the device name is up to 256 characters
         snprintf(buf, sizeof buf, "CUDA device %d (%s, sm_%d%d): the kernels are built for sm_100a (B200)", device,
                  p.name, p.major, p.minor);
         return fail(JK_ERR_UNSUPPORTED, buf);

@@ -284,6 +284,74 @@ def grouped_bench(gpu, dev, timed, pk):
             "workloads": results}
 
 
+HEAD_VOCAB = 262144  # token-table rows of the head workloads (the Gemma vocabulary)
+
+
+def head_bench(gpu, dev, timed, pk):
+    """The Q6_K embedding-table operators on a [HEAD_VOCAB, K_DIM] table of synthetic Q6_K blocks:
+    the dequantized f16 transpose of the whole table (HBM-bound: reads the 551 MB table, writes
+    the 1.34 GB transpose), candidate logits for 16 rows x 256 candidates, and 512 embedding rows
+    (canvas rows with self-conditioning input). CUDA graph replay, CUDA events."""
+    import torch
+    from jevons_kernels import head
+    from jevons_kernels.formats import TensorType
+    from jevons_kernels.gemm import Buf, QMatrix
+
+    rng = np.random.default_rng(21)
+    vocab, d = HEAD_VOCAB, K_DIM
+    nb = vocab * d // 256
+    raw = np.empty((nb, 210), np.uint8)
+    raw[:, :192] = rng.integers(0, 256, size=(nb, 192), dtype=np.uint8)
+    raw[:, 192:208] = rng.integers(-99, 100, size=(nb, 16)).astype(np.int8).view(np.uint8)
+    raw[:, 208:210] = (0.001 + rng.random(nb) * 0.01).astype(np.float16).view(np.uint8).reshape(nb, 2)
+    table = QMatrix.upload(gpu, TensorType.Q6K, vocab, d, 1, raw.reshape(-1))
+    del raw
+    table_bytes = vocab * d // 256 * 210
+    res = {}
+
+    out_t = torch.empty(vocab * d, dtype=torch.float16, device=dev)
+    tbuf = Buf(out_t)
+
+    def transpose():
+        head.q6k_transposed_f16(gpu, table, vocab, d, out=tbuf)
+    steps = 20
+    ms = timed(transpose, steps, 3) / steps
+    alg = table_bytes + vocab * d * 2
+    res["q6k_transpose_f16"] = {"us": ms * 1e3, "algorithmic_bytes": alg, "gbs": alg / (ms * 1e-3) / 1e9,
+                                "frac_of_hbm": alg / (ms * 1e-3) / 1e9 / pk["hbm_gbs"]}
+    del out_t, tbuf
+
+    rows, cands, cap = 16, 256, 30.0
+    x16 = torch.from_numpy(rng.uniform(-1, 1, (rows, d)).astype(np.float16)).to(dev)
+    pairs_np = np.stack([np.repeat(np.arange(rows), cands), rng.integers(0, vocab, rows * cands)], 1)
+    pairs = torch.from_numpy(pairs_np.astype(np.int32).reshape(-1)).to(dev)
+    logits = torch.empty(rows * cands, device=dev)
+    xb, pb, lb = Buf(x16), Buf(pairs), Buf(logits)
+
+    def pick():
+        head.pick(gpu, xb, pb, rows * cands, table, lb, cap, d)
+    steps = 200
+    ms = timed(pick, steps, 3) / steps
+    rb = rows * cands * d // 256 * 210
+    res["pick_logits"] = {"us": ms * 1e3, "pairs": rows * cands, "table_row_gbs": rb / (ms * 1e-3) / 1e9}
+
+    n_tok, first = 512, 0
+    toks = torch.from_numpy(rng.integers(0, vocab, n_tok).astype(np.int32)).to(dev)
+    w_attn = torch.from_numpy(rng.uniform(-1, 1, d).astype(np.float32)).to(dev)
+    cond = torch.from_numpy(rng.uniform(-1, 1, (n_tok, d)).astype(np.float32)).to(dev)
+    eo = torch.empty(n_tok * d, device=dev)
+    ex = torch.empty(n_tok * d, dtype=torch.float16, device=dev)
+    tb_, wb_, cb_, eob, exb = Buf(toks), Buf(w_attn), Buf(cond), Buf(eo), Buf(ex)
+
+    def embed():
+        head.embed(gpu, tb_, table, wb_, cb_, eob, exb, n_tok, first, d, 1e-6)
+    ms = timed(embed, steps, 3) / steps
+    eb = n_tok * (d // 256 * 210 + d * 4 + d * 4 + d * 2)
+    res["embed_q6k"] = {"us": ms * 1e3, "rows": n_tok, "gbs": eb / (ms * 1e-3) / 1e9}
+    return {"what": f"Q6_K table [{vocab}, {d}] (synthetic blocks); CUDA graph replay, CUDA events; "
+                    "transpose bytes = table read + f16 transpose written", "ops": res}
+
+
 def run_ours(args):
     import torch
     world = int(os.environ.get("WORLD_SIZE", "1"))
@@ -439,6 +507,9 @@ def run_ours(args):
     grouped = None
     if world == 1 and not args.no_grouped:
         grouped = grouped_bench(gpu, dev, timed, pk)
+    head_ops = None
+    if world == 1 and not args.no_head:
+        head_ops = head_bench(gpu, dev, timed, pk)
 
     cpu = None
     if rank == 0 and world == 1 and not args.no_cpu_baseline:
@@ -468,6 +539,7 @@ def run_ours(args):
             "m32": {"metric": "Q4_K GEMM TFLOP/s (M=32, BASELINE config 1)", "value": m32_tflops, "unit": "TFLOP/s",
                     "weight_gbs": wbytes * L * gv_steps * world / (c_ms * 1e-3) / 1e9},
             "grouped": grouped,
+            "head": head_ops,
             "e2e": {"value": e2e_value, "unit": "TFLOP/s", "h2d_bytes_per_step": xh.numel() * 2,
                     "d2h_bytes_per_step": oh.numel() * 4},
             "gpu_launches": args.steps * L * launches_per_product,
@@ -492,6 +564,7 @@ def main():
     ap.add_argument("--layers", type=int, default=LAYERS)
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--no-grouped", action="store_true", help="skip the expert-grouped workloads")
+    ap.add_argument("--no-head", action="store_true", help="skip the Q6_K embedding-table workloads")
     args = ap.parse_args()
     if args.warmup < 3:
         args.warmup = 3

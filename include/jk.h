@@ -270,6 +270,46 @@ jk_status jk_matvec_grouped(const jk_qmatrix *w, const void *x, int x_dtype, siz
 jk_status jk_matmul_splitk_noalloc(const jk_qmatrix *w, const void *x, int x_dtype, size_t x_len, size_t m,
                                    float *out, size_t out_len, int bm, void *stream);
 
+/* ---- Q6_K embedding-table ("head") operators --------------------------------------------------
+ * `table` is a Q6_K matrix [vocab, d] (experts * n rows, k = d): the model's token embedding and
+ * tied output projection. The reference passes the same data as the packed word regions of
+ * ops::Q6kTable (crates/jevons-gemma4-diffusion/src/gpu/ops.rs:912-919, model.rs:181-184); here
+ * it is a jk_qmatrix (jk_qmatrix_upload / jk_qmatrix_from_packed of type JK_TYPE_Q6_K). All device
+ * pointers; all calls asynchronous on `stream`. Errors: JK_ERR_UNSUPPORTED for a table that is
+ * not Q6_K; JK_ERR_INVALID for null or misaligned buffers. Ids outside the table or rows outside
+ * x are found on the device: they set an error bit (2) that jk_device_error reports, instead of
+ * being read out of bounds. */
+
+/* ops::embed (ops.rs:921-954; kernel embed_q6k :223-291). For t < rows:
+ *   out[t]    = E[tokens[t]] * sqrt(d)                                      f32 [rows, d]
+ *   rows t >= first_canvas then add cond[t - first_canvas] (f32 [rows - first_canvas, d]) when
+ *   cond_dev is not NULL and are RMS-normalised without weight:  out[t] *= 1/sqrt(mean(out[t]^2) + eps)
+ *   x_attn[t] = f16(out[t] * 1/sqrt(mean(out[t]^2) + eps) * w_attn)        f16 [rows, d]
+ * The pre-normalisation values are bit-exact with the reference (exact decode, one rounding by
+ * sqrt(d)). d <= 16384 (JK_ERR_SHAPE above). w_attn, cond, out, x_attn 16-byte aligned. A token
+ * id >= vocab computes its row from zeros. */
+jk_status jk_embed_q6k(const jk_qmatrix *table, const uint32_t *tokens_dev, size_t rows, const float *w_attn_dev,
+                       const float *cond_dev, size_t first_canvas, float eps, float *out_dev, void *x_attn_f16_dev,
+                       void *stream);
+
+/* ops::pick (ops.rs:1133-1157; kernel pick_logits :590-635): for p < count, with
+ * (row, token) = (pairs[2p], pairs[2p+1]):  out[p] = softcap * tanh(dot(x[row], E[token]) / softcap)
+ * x is f16 [x_rows, d] (16-byte aligned), out f32 [count]. A pair outside x or the table writes
+ * NaN. */
+jk_status jk_pick_logits(const jk_qmatrix *table, const void *x_f16_dev, size_t x_rows, const uint32_t *pairs_dev,
+                         size_t count, float softcap, float *out_dev, void *stream);
+
+/* ops::q6k_transposed_f16 (ops.rs:732-749; kernel q6k_transpose :672-715): the dequantized table
+ * transposed to f16 [d, vocab] (out_len = vocab * d values, 16-byte aligned), bit-exact with
+ * f16(quant::dequantize) transposed. vocab % 64 == 0 (JK_ERR_SHAPE otherwise), as the reference
+ * asserts. */
+jk_status jk_q6k_transpose_f16(const jk_qmatrix *table, void *out_f16_dev, size_t out_len, void *stream);
+
+/* ops::softcap_logits (ops.rs:1159-1168; kernel softcap :751-760): x[i] = cap * tanh(x[i] / cap)
+ * in place for i < len, on the current device (x 16-byte aligned). With jk_matmul over the table
+ * this is the reference's full-vocabulary head (model.rs:1192-1205). */
+jk_status jk_softcap(float *x_dev, size_t len, float cap, void *stream);
+
 #ifdef __cplusplus
 }
 #endif

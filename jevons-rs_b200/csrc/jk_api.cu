@@ -122,18 +122,7 @@ uint16_t float_to_half(float f) {
     return (uint16_t)(sign | r);
 }
 
-struct DeviceGuard {
-    int prev = -1;
-    bool changed = false;
-    explicit DeviceGuard(int dev) {
-        if (cudaGetDevice(&prev) == cudaSuccess && prev != dev) {
-            changed = cudaSetDevice(dev) == cudaSuccess;
-        }
-    }
-    ~DeviceGuard() {
-        if (changed) cudaSetDevice(prev);
-    }
-};
+using jk::DeviceGuard;
 
 // Runs f(begin, end) over [0, count) on up to 16 host threads (host-side repacking).
 template <class F>

@@ -32,6 +32,18 @@ struct jk_split_scratch {
 
 namespace jk {
 
+// Makes `dev` the current device for the scope and restores the previous one.
+struct DeviceGuard {
+    int prev = -1;
+    bool changed = false;
+    explicit DeviceGuard(int dev) {
+        if (cudaGetDevice(&prev) == cudaSuccess && prev != dev) changed = cudaSetDevice(dev) == cudaSuccess;
+    }
+    ~DeviceGuard() {
+        if (changed) cudaSetDevice(prev);
+    }
+};
+
 // Thread-local error message; returns `st` for convenient `return fail(...)`.
 jk_status fail(jk_status st, const std::string& msg);
 jk_status cuda_fail(cudaError_t e, const char* what);

@@ -70,6 +70,10 @@ SIGNATURES = {
     "jk_group_experts": (I, [I, P, S, S, I, P, P, P, S, P]),
     "jk_matmul_grouped": (I, [P, P, I, S, ctypes.POINTER(Groups), P, S, I, I, I, P, P]),
     "jk_matvec_grouped": (I, [P, P, I, S, ctypes.POINTER(Groups), P, S, I, P]),
+    "jk_embed_q6k": (I, [P, P, S, P, P, S, ctypes.c_float, P, P, P]),
+    "jk_pick_logits": (I, [P, P, S, P, S, ctypes.c_float, P, P]),
+    "jk_q6k_transpose_f16": (I, [P, P, S, P]),
+    "jk_softcap": (I, [P, S, ctypes.c_float, P]),
 }
 
 STATUS = {0: "JK_OK", 1: "JK_ERR_INVALID", 2: "JK_ERR_UNSUPPORTED", 3: "JK_ERR_SHAPE", 4: "JK_ERR_CUDA",

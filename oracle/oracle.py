@@ -298,3 +298,52 @@ def matmul_grouped_f64(x: np.ndarray, w_dense: np.ndarray, n: int, ids, in_div: 
         rows = np.nonzero(ids == e)[0]
         out[rows] = matmul_f64(x[rows // in_div], w_dense[e * n:(e + 1) * n])
     return out
+
+
+# ---- Q6_K embedding-table ("head") operators ----------------------------------------------------
+# Definitions of crates/jevons-gemma4-diffusion/src/gpu/ops.rs (embed_q6k :223-291, pick_logits
+# :590-635, q6k_transpose :672-715, softcap :751-760), evaluated as the reference's own test does
+# (crates/jevons-gemma4-diffusion/src/gpu/tests.rs:556-648): the table is quant::dequantize of the
+# Q6_K bytes, sums and norms in f64.
+
+def embed_rows_f32(table: np.ndarray, tokens) -> np.ndarray:
+    """embed_q6k before any normalisation: `dq*s*(q-32)*sqrt(d)` in f32 (ops.rs:249-270); the
+    decoded weight is exact, so this is one f32 rounding of table[token] * f32(sqrt(d))."""
+    d = table.shape[1]
+    return table[np.asarray(tokens, dtype=np.int64)] * np.float32(np.sqrt(np.float32(d)))
+
+
+def _rms_norm_f64(x: np.ndarray, eps: float) -> np.ndarray:
+    r = 1.0 / np.sqrt((x * x).sum(axis=-1, keepdims=True) / x.shape[-1] + np.float64(np.float32(eps)))
+    return x * r
+
+
+def embed_q6k_f64(table: np.ndarray, tokens, w_attn: np.ndarray, cond, first_canvas: int, eps: float):
+    """(out, x_attn) of embed_q6k (ops.rs:223-291) in f64, as tests.rs:591-619 evaluates them:
+    row = E[token] * sqrt(d); canvas rows (index >= first_canvas) add cond[index - first_canvas]
+    when given and are RMS-normalised; x_attn = norm(row) * w_attn."""
+    d = table.shape[1]
+    rows = table[np.asarray(tokens, dtype=np.int64)].astype(np.float64) * np.sqrt(np.float64(d))
+    for i in range(first_canvas, rows.shape[0]):
+        if cond is not None:
+            rows[i] += np.asarray(cond, np.float64).reshape(-1, d)[i - first_canvas]
+        rows[i] = _rms_norm_f64(rows[i], eps)
+    return rows, _rms_norm_f64(rows, eps) * np.asarray(w_attn, np.float64)
+
+
+def pick_logits_f64(table: np.ndarray, x_f16: np.ndarray, pairs, cap: float) -> np.ndarray:
+    """pick_logits (ops.rs:590-635) as tests.rs:636-646 evaluates it: cap * tanh(x[row].E[token] / cap)."""
+    pr = np.asarray(pairs, dtype=np.int64).reshape(-1, 2)
+    x64 = np.asarray(x_f16, np.float32).astype(np.float64)
+    dots = np.einsum("pd,pd->p", x64[pr[:, 0]], table[pr[:, 1]].astype(np.float64))
+    return np.float64(cap) * np.tanh(dots / np.float64(cap))
+
+
+def q6k_transpose_f16(table: np.ndarray) -> np.ndarray:
+    """q6k_transpose (ops.rs:672-715): f16 (round to nearest even) of the table, transposed to [d, rows]."""
+    return np.ascontiguousarray(table.astype(np.float16).T)
+
+
+def softcap_f64(x: np.ndarray, cap: float) -> np.ndarray:
+    """softcap (ops.rs:751-760): cap * tanh(x / cap)."""
+    return np.float64(cap) * np.tanh(np.asarray(x, np.float64) / np.float64(cap))

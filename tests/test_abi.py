@@ -104,3 +104,16 @@ def test_pack_rejects_small_regions():
     st = load().jk_pack(8, raw.ctypes.data_as(ctypes.c_void_p), 34, q.ctypes.data_as(ctypes.c_void_p), 7, None, 0,
                         None, 0, d.ctypes.data_as(ctypes.c_void_p), 1)
     assert st == 1
+
+
+def test_head_operators_reject_null_arguments_without_a_device():
+    lib = load()
+    null = ctypes.c_void_p(0)
+    assert lib.jk_embed_q6k(null, null, 1, null, null, 0, ctypes.c_float(1e-6), null, null, null) == 1
+    assert lib.jk_last_error().decode() == "embed_q6k: null table"
+    assert lib.jk_pick_logits(null, null, 1, null, 1, ctypes.c_float(30.0), null, null) == 1
+    assert lib.jk_last_error().decode() == "pick_logits: null table"
+    assert lib.jk_q6k_transpose_f16(null, null, 0, null) == 1
+    assert lib.jk_softcap(null, 4, ctypes.c_float(30.0), null) == 1
+    assert "softcap" in lib.jk_last_error().decode()
+    assert lib.jk_softcap(null, 0, ctypes.c_float(30.0), null) == 0  # nothing to do

@@ -209,3 +209,26 @@ def test_grouped_product_definition():
         for c in range(n):
             want = sum(float(x[a // top_k, i]) * float(w[e * n + c, i]) for i in range(k))
             assert abs(got[a, c] - want) <= 1e-12 * max(1.0, abs(want))
+
+
+def test_head_oracle_follows_the_reference_test_definitions():
+    """The head operators' oracle (ops.rs:223-291, 590-635, 672-715 as tests.rs:556-648 checks
+    them): plain rows are table rows times sqrt(d), canvas rows have unit RMS, the transposed table
+    is the f16 of the dequantized table, pick is a capped dot product."""
+    rng = np.random.default_rng(11)
+    vocab, d, eps = 64, 512, 1e-6
+    raw = synth.q6k_blocks(rng, vocab, d)
+    dense = oracle.dequantize(oracle.Q6_K, raw).reshape(vocab, d)
+    tokens = [3, 9, 63, 0]
+    w = np.ones(d, np.float32)
+    out, xn = oracle.embed_q6k_f64(dense, tokens, w, None, 2, eps)
+    exact = oracle.embed_rows_f32(dense, tokens)
+    assert np.allclose(out[:2], exact[:2], rtol=1e-7, atol=0)
+    assert np.allclose(np.sqrt((out[2:] ** 2).mean(axis=1)), 1.0, rtol=1e-5)
+    assert np.allclose(xn, out / np.sqrt((out ** 2).mean(axis=1, keepdims=True) + eps), rtol=1e-12)
+    t = oracle.q6k_transpose_f16(dense)
+    assert t.shape == (d, vocab) and t.dtype == np.float16 and t[5, 7] == np.float16(dense[7, 5])
+    x = rng.standard_normal((2, d)).astype(np.float16)
+    got = oracle.pick_logits_f64(dense, x, [1, 4, 0, 60], 30.0)
+    dot = float(np.dot(x[1].astype(np.float64), dense[4].astype(np.float64)))
+    assert got[0] == pytest.approx(30.0 * np.tanh(dot / 30.0), rel=1e-12)

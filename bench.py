@@ -287,7 +287,7 @@ def grouped_bench(gpu, dev, timed, pk):
 HEAD_VOCAB = 262144  # token-table rows of the head workloads (the Gemma vocabulary)
 
 
-def head_bench(gpu, dev, timed, pk):
+def head_bench(gpu, dev, timed, pk, vocab: int = HEAD_VOCAB):
     """The Q6_K embedding-table operators on a [HEAD_VOCAB, K_DIM] table of synthetic Q6_K blocks:
     the dequantized f16 transpose of the whole table (HBM-bound: reads the 551 MB table, writes
     the 1.34 GB transpose), candidate logits for 16 rows x 256 candidates, and 512 embedding rows
@@ -298,7 +298,7 @@ def head_bench(gpu, dev, timed, pk):
     from jevons_kernels.gemm import Buf, QMatrix
 
     rng = np.random.default_rng(21)
-    vocab, d = HEAD_VOCAB, K_DIM
+    d = K_DIM
     nb = vocab * d // 256
     raw = np.empty((nb, 210), np.uint8)
     raw[:, :192] = rng.integers(0, 256, size=(nb, 192), dtype=np.uint8)
@@ -350,6 +350,40 @@ def head_bench(gpu, dev, timed, pk):
     res["embed_q6k"] = {"us": ms * 1e3, "rows": n_tok, "gbs": eb / (ms * 1e-3) / 1e9}
     return {"what": f"Q6_K table [{vocab}, {d}] (synthetic blocks); CUDA graph replay, CUDA events; "
                     "transpose bytes = table read + f16 transpose written", "ops": res}
+
+
+def run_head_only(args):
+    """`--head-only`: the Q6_K table workloads alone (one GPU), for profiling them; prints the
+    head object of the bench line."""
+    import torch
+    from jevons_kernels.gemm import Gpu
+
+    gpu = Gpu(0)
+    dev = torch.device("cuda", 0)
+    graphs = []
+
+    def timed(fn, steps, warmup):
+        for _ in range(warmup):
+            fn()
+        torch.cuda.synchronize()
+        g = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(g):
+            fn()
+        graphs.append(g)
+        g.replay()
+        torch.cuda.synchronize()
+        a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        a.record()
+        for _ in range(steps):
+            g.replay()
+        b.record()
+        torch.cuda.synchronize()
+        return a.elapsed_time(b)
+
+    pk, _ = peaks()
+    print(json.dumps({"head": head_bench(gpu, dev, timed, pk, args.head_vocab)}), flush=True)
+    graphs.clear()
+    return 0
 
 
 def run_ours(args):
@@ -565,11 +599,15 @@ def main():
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--no-grouped", action="store_true", help="skip the expert-grouped workloads")
     ap.add_argument("--no-head", action="store_true", help="skip the Q6_K embedding-table workloads")
+    ap.add_argument("--head-only", action="store_true", help="run only the Q6_K embedding-table workloads")
+    ap.add_argument("--head-vocab", type=int, default=HEAD_VOCAB, help="table rows of the head workloads")
     args = ap.parse_args()
     if args.warmup < 3:
         args.warmup = 3
     if args.impl == "reference":
         return run_reference(args)
+    if args.head_only:
+        return run_head_only(args)
     return run_ours(args)
 
 

@@ -310,6 +310,49 @@ jk_status jk_q6k_transpose_f16(const jk_qmatrix *table, void *out_f16_dev, size_
  * this is the reference's full-vocabulary head (model.rs:1192-1205). */
 jk_status jk_softcap(float *x_dev, size_t len, float cap, void *stream);
 
+/* ---- measured launch plans ---------------------------------------------------------------------
+ * Tuner (crates/jevons-gemma4-diffusion/src/gpu/tune.rs): plans for the dense products timed on
+ * the device, keyed by (type, n, k, row bucket, row invariance), stored in a text file keyed by a
+ * device profile (name, SM count, compute capability, shared memory, L2, library ABI). A tuner is
+ * used from one thread at a time for tuning; lookups are thread safe. */
+
+typedef struct jk_tuner jk_tuner;
+
+/* bucket (tune.rs:74-76): plans measured at m = bucket serve every m in (bucket/2, bucket];
+ * the next power of two, at least 4. */
+size_t jk_tune_bucket(size_t m);
+
+/* pick (tune.rs:548-562): the fastest of `count` timed plans, unless `baseline` (the heuristic)
+ * is among them and within 5% of it -- then the baseline, so noise changes nothing. */
+jk_status jk_tune_pick(const double *times, const jk_plan *plans, size_t count, jk_plan baseline, jk_plan *out);
+
+/* Tuner::new (tune.rs:139-155): a plan table for `device`. `path` (NULL = memory only) is the file
+ * jk_tuner_save writes; with `load` != 0 its entries are read first when its profile line matches
+ * this device and library (otherwise the file is ignored, as the reference does). */
+jk_status jk_tuner_create(int device, const char *path, int load, jk_tuner **out);
+void jk_tuner_destroy(jk_tuner *t);
+/* Number of stored plans. */
+size_t jk_tuner_size(const jk_tuner *t);
+
+/* Tuner::dense (tune.rs:162-175): the stored plan for w's type and shape and bucket(m) if it is
+ * valid for m (and has no split-K when row_invariant), else jk_plan_heuristic(w, m, row_invariant). */
+jk_status jk_tuner_plan(const jk_tuner *t, const jk_qmatrix *w, size_t m, int row_invariant, jk_plan *out);
+
+/* Tuner::tune_dense (tune.rs:231-269): times the candidate plans (bm 32..256 no taller than
+ * needed, bn 128/256, splits 1/2/4/8 unless row_invariant; the GEMV plan for m <= JK_GEMV_ROWS)
+ * at m = bucket(m) rows, running the product over all `count` matrices (same type and shape;
+ * pass enough of them to exceed the L2 cache, so weights stream from HBM as in a forward pass),
+ * and stores the pick. x / out hold bucket(m) rows (contents overwritten); scratch as for
+ * jk_matmul_plan. Timing: CUDA events on `stream`, best of 3 batches of >= 2 ms. Synchronises
+ * the stream. *chosen (may be NULL) receives the stored plan. */
+jk_status jk_tuner_tune(jk_tuner *t, const jk_qmatrix *const *ws, size_t count, size_t m, int row_invariant,
+                        const void *x, int x_dtype, size_t x_len, float *out, size_t out_len,
+                        jk_split_scratch *scratch, void *stream, jk_plan *chosen);
+
+/* Tuner::save (tune.rs:412-446): writes the profile line and one "dense <type> <n> <k> <bucket>
+ * <row_invariant> <bm> <bn> <splits>" line per plan to path (through path.tmp and a rename). */
+jk_status jk_tuner_save(const jk_tuner *t);
+
 #ifdef __cplusplus
 }
 #endif

@@ -74,6 +74,14 @@ SIGNATURES = {
     "jk_pick_logits": (I, [P, P, S, P, S, ctypes.c_float, P, P]),
     "jk_q6k_transpose_f16": (I, [P, P, S, P]),
     "jk_softcap": (I, [P, S, ctypes.c_float, P]),
+    "jk_tune_bucket": (S, [S]),
+    "jk_tune_pick": (I, [ctypes.POINTER(ctypes.c_double), ctypes.POINTER(Plan), S, Plan, ctypes.POINTER(Plan)]),
+    "jk_tuner_create": (I, [I, ctypes.c_char_p, I, ctypes.POINTER(P)]),
+    "jk_tuner_destroy": (None, [P]),
+    "jk_tuner_size": (S, [P]),
+    "jk_tuner_plan": (I, [P, P, S, I, ctypes.POINTER(Plan)]),
+    "jk_tuner_tune": (I, [P, ctypes.POINTER(P), S, S, I, P, I, S, P, S, P, P, ctypes.POINTER(Plan)]),
+    "jk_tuner_save": (I, [P]),
 }
 
 STATUS = {0: "JK_OK", 1: "JK_ERR_INVALID", 2: "JK_ERR_UNSUPPORTED", 3: "JK_ERR_SHAPE", 4: "JK_ERR_CUDA",

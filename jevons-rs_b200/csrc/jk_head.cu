@@ -207,14 +207,17 @@ __global__ void __launch_bounds__(32 * PICK_WARPS) pick_logits_kernel(WView t, c
 // the output rows c and c+1; a warp writes four 128-byte output row segments per step.
 constexpr int TR_ROWS = 64;
 
-__global__ void __launch_bounds__(256) q6k_transpose_kernel(WView t, __half* __restrict__ out) {
+// Six CTAs per SM and all eight rows' loads of a warp issued before any decode: the kernel is
+// bound by load latency (long-scoreboard stalls) at fewer bytes in flight. blockIdx.x is the
+// super-block column, so the CTAs resident together read whole table rows.
+__global__ void __launch_bounds__(256, 6) q6k_transpose_kernel(WView t, __half* __restrict__ out) {
     __shared__ __align__(16) uint8_t tile[TR_ROWS * 512];
-    const int64_t r0 = (int64_t)blockIdx.x * TR_ROWS;
-    const int sb = blockIdx.y;
+    const int64_t r0 = (int64_t)blockIdx.y * TR_ROWS;
+    const int sb = blockIdx.x;
     const int64_t vocab = t.rows;
     const int sbs = (int)(t.k >> 8);
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-#pragma unroll 4
+#pragma unroll
     for (int i = 0; i < TR_ROWS / 8; ++i) {
         const int r = warp + 8 * i;
         const int64_t row = r0 + r;
@@ -342,10 +345,10 @@ extern "C" jk_status jk_q6k_transpose_f16(const jk_qmatrix* table, void* out_f16
     if (vocab == 0) return JK_OK;
     if (!out_f16_dev || !jk::aligned16(out_f16_dev))
         return fail(JK_ERR_INVALID, "q6k_transpose: output must be a 16-byte aligned device buffer");
-    if (vocab / jk::TR_ROWS > (size_t)INT32_MAX || d / 256 > 65535)
-        return fail(JK_ERR_SHAPE, "q6k_transpose: table too large");
+    if (vocab / jk::TR_ROWS > 65535 || d / 256 > (size_t)INT32_MAX)
+        return fail(JK_ERR_SHAPE, "q6k_transpose: table above 4194240 rows");
     DeviceGuard g(table->device);
-    const dim3 grid((unsigned)(vocab / jk::TR_ROWS), (unsigned)(d / 256));
+    const dim3 grid((unsigned)(d / 256), (unsigned)(vocab / jk::TR_ROWS));
     jk::q6k_transpose_kernel<<<grid, 256, 0, static_cast<cudaStream_t>(stream)>>>(table->view,
                                                                                 static_cast<__half*>(out_f16_dev));
     return jk::launched("q6k_transpose launch");

@@ -310,6 +310,59 @@ jk_status jk_q6k_transpose_f16(const jk_qmatrix *table, void *out_f16_dev, size_
  * this is the reference's full-vocabulary head (model.rs:1192-1205). */
 jk_status jk_softcap(float *x_dev, size_t len, float cap, void *stream);
 
+/* ---- GGUF reader and weight loader --------------------------------------------------------------
+ * Gguf (crates/jevons-formats/src/gguf.rs:164-391), host only. Errors are JK_ERR_INVALID with the
+ * reference's texts: "Invalid GGUF file: <why>", "I/O error reading the model: <why>",
+ * "Missing GGUF metadata key <key>", "Missing tensor <name>". */
+
+typedef struct jk_gguf jk_gguf;
+
+/* TensorInfo (gguf.rs:148-156). dims in GGML order (dims[0] = contiguous row length), unused dims
+ * 1; offset is absolute in the file; bytes = 0 for types without a block size. `name` is valid
+ * until jk_gguf_close. */
+typedef struct jk_gguf_tensor_info {
+    const char *name;
+    uint32_t n_dims;
+    uint64_t dims[4];
+    int32_t type;
+    uint64_t offset;
+    uint64_t bytes;
+} jk_gguf_tensor_info;
+
+/* Gguf::open (gguf.rs:234-324): parses and validates the header (magic, version 2 or 3, at most
+ * 2^20 tensors and keys, metadata of the 13 GGUF kinds without nested arrays, strings <= 2^24
+ * bytes of UTF-8, arrays <= 2^26 values, general.alignment a power of two (default 32), 1..4 dims,
+ * block-aligned rows, every tensor aligned and inside the file, no duplicate keys or names). */
+jk_status jk_gguf_open(const char *path, jk_gguf **out);
+void jk_gguf_close(jk_gguf *g);
+size_t jk_gguf_tensor_count(const jk_gguf *g);
+size_t jk_gguf_metadata_count(const jk_gguf *g);
+/* Tensor i in file order / Gguf::tensor (gguf.rs:345-350) by name. */
+jk_status jk_gguf_tensor_at(const jk_gguf *g, size_t i, jk_gguf_tensor_info *out);
+jk_status jk_gguf_tensor(const jk_gguf *g, const char *name, jk_gguf_tensor_info *out);
+/* Gguf::read_range (gguf.rs:365-372; Gguf::read with start 0, len = bytes): raw bytes of a tensor
+ * of a supported type ("tensor <name> has unsupported type Other(<id>)" otherwise). */
+jk_status jk_gguf_read(const jk_gguf *g, const char *name, uint64_t start, uint64_t len, void *dst);
+/* Gguf::read_f32 (gguf.rs:374-391): an F32 tensor's values (dst holds bytes / 4 floats). */
+jk_status jk_gguf_read_f32(const jk_gguf *g, const char *name, float *dst, size_t dst_len);
+
+/* Metadata. kind: the GGUF value type (0 u8 .. 12 f64; 8 string, 9 array); for arrays elem_kind
+ * and len (values), for strings len (bytes), else len 1. The getters read the value at `key`, or
+ * element `index` of the array at `key` when index >= 0, with Value::as_u64 / as_i64 / as_f64 /
+ * as_bool / as_str semantics (gguf.rs:53-105; Gguf::u64 / f32, :332-343). Strings stay valid until
+ * jk_gguf_close. */
+jk_status jk_gguf_value_kind(const jk_gguf *g, const char *key, int *kind, int *elem_kind, size_t *len);
+jk_status jk_gguf_u64(const jk_gguf *g, const char *key, int64_t index, uint64_t *out);
+jk_status jk_gguf_i64(const jk_gguf *g, const char *key, int64_t index, int64_t *out);
+jk_status jk_gguf_f32(const jk_gguf *g, const char *key, int64_t index, float *out);
+jk_status jk_gguf_bool(const jk_gguf *g, const char *key, int64_t index, int *out);
+jk_status jk_gguf_str(const jk_gguf *g, const char *key, int64_t index, const char **out, size_t *len);
+
+/* The model load path for one weight: reads the tensor's raw GGML blocks and uploads them with
+ * jk_qmatrix_upload as [experts * n, k] with k = dims[0], n = dims[1], experts = dims[2] * dims[3]
+ * (the reference's per-layer and expert tensors). */
+jk_status jk_qmatrix_from_gguf(int device, const jk_gguf *g, const char *name, jk_qmatrix **out);
+
 /* ---- measured launch plans ---------------------------------------------------------------------
  * Tuner (crates/jevons-gemma4-diffusion/src/gpu/tune.rs): plans for the dense products timed on
  * the device, keyed by (type, n, k, row bucket, row invariance), stored in a text file keyed by a

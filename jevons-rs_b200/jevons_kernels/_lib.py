@@ -37,6 +37,13 @@ class Groups(ctypes.Structure):
                 ("max_jobs", ctypes.c_size_t), ("in_div", ctypes.c_uint32), ("rows", ctypes.c_size_t)]
 
 
+class GgufTensorInfo(ctypes.Structure):
+    """jk_gguf_tensor_info: TensorInfo (crates/jevons-formats/src/gguf.rs:148-156)."""
+
+    _fields_ = [("name", ctypes.c_char_p), ("n_dims", ctypes.c_uint32), ("dims", ctypes.c_uint64 * 4),
+                ("type", ctypes.c_int32), ("offset", ctypes.c_uint64), ("bytes", ctypes.c_uint64)]
+
+
 SIGNATURES = {
     "jk_last_error": (ctypes.c_char_p, []),
     "jk_abi_version": (I, []),
@@ -74,6 +81,21 @@ SIGNATURES = {
     "jk_pick_logits": (I, [P, P, S, P, S, ctypes.c_float, P, P]),
     "jk_q6k_transpose_f16": (I, [P, P, S, P]),
     "jk_softcap": (I, [P, S, ctypes.c_float, P]),
+    "jk_gguf_open": (I, [ctypes.c_char_p, ctypes.POINTER(P)]),
+    "jk_gguf_close": (None, [P]),
+    "jk_gguf_tensor_count": (S, [P]),
+    "jk_gguf_metadata_count": (S, [P]),
+    "jk_gguf_tensor_at": (I, [P, S, ctypes.POINTER(GgufTensorInfo)]),
+    "jk_gguf_tensor": (I, [P, ctypes.c_char_p, ctypes.POINTER(GgufTensorInfo)]),
+    "jk_gguf_read": (I, [P, ctypes.c_char_p, U64, U64, P]),
+    "jk_gguf_read_f32": (I, [P, ctypes.c_char_p, P, S]),
+    "jk_gguf_value_kind": (I, [P, ctypes.c_char_p, ctypes.POINTER(I), ctypes.POINTER(I), ctypes.POINTER(S)]),
+    "jk_gguf_u64": (I, [P, ctypes.c_char_p, ctypes.c_int64, ctypes.POINTER(U64)]),
+    "jk_gguf_i64": (I, [P, ctypes.c_char_p, ctypes.c_int64, ctypes.POINTER(ctypes.c_int64)]),
+    "jk_gguf_f32": (I, [P, ctypes.c_char_p, ctypes.c_int64, ctypes.POINTER(ctypes.c_float)]),
+    "jk_gguf_bool": (I, [P, ctypes.c_char_p, ctypes.c_int64, ctypes.POINTER(I)]),
+    "jk_gguf_str": (I, [P, ctypes.c_char_p, ctypes.c_int64, ctypes.POINTER(ctypes.c_char_p), ctypes.POINTER(S)]),
+    "jk_qmatrix_from_gguf": (I, [I, P, ctypes.c_char_p, ctypes.POINTER(P)]),
     "jk_tune_bucket": (S, [S]),
     "jk_tune_pick": (I, [ctypes.POINTER(ctypes.c_double), ctypes.POINTER(Plan), S, Plan, ctypes.POINTER(Plan)]),
     "jk_tuner_create": (I, [I, ctypes.c_char_p, I, ctypes.POINTER(P)]),

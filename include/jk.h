@@ -402,8 +402,23 @@ jk_status jk_tuner_tune(jk_tuner *t, const jk_qmatrix *const *ws, size_t count, 
                         const void *x, int x_dtype, size_t x_len, float *out, size_t out_len,
                         jk_split_scratch *scratch, void *stream, jk_plan *chosen);
 
-/* Tuner::save (tune.rs:412-446): writes the profile line and one "dense <type> <n> <k> <bucket>
- * <row_invariant> <bm> <bn> <splits>" line per plan to path (through path.tmp and a rename). */
+/* Tuner::grouped (tune.rs:177-192): the stored grouped tile {bm, bn, 1} for w (type, n, k, experts)
+ * and bucket(rows) when n is a multiple of its bn, else the default {32, 128, 1}. */
+jk_status jk_tuner_group_plan(const jk_tuner *t, const jk_qmatrix *w, size_t rows, jk_plan *out);
+
+/* Tuner::tune_grouped (tune.rs:271-346): for m tokens routed top_k ways, groups the first
+ * a = bucket(m) * top_k ids of `ids` (device, < experts) for each candidate tile (bm 32/64/128/256
+ * x bn 128/256) with jk_group_experts into sorted / offsets / jobs (jobs_len as for that call at
+ * bm 32), times jk_matmul_grouped over the `count` expert matrices (x: a rows, one per route) and
+ * stores the pick against the default {32, 128}. Synchronises the stream. */
+jk_status jk_tuner_tune_grouped(jk_tuner *t, const jk_qmatrix *const *ws, size_t count, size_t m, size_t top_k,
+                                const uint32_t *ids, size_t ids_len, const void *x, int x_dtype, size_t x_len,
+                                float *out, size_t out_len, uint32_t *sorted, uint32_t *offsets, uint32_t *jobs,
+                                size_t jobs_len, jk_split_scratch *scratch, void *stream, jk_plan *chosen);
+
+/* Tuner::save (tune.rs:412-446): writes the profile line, one "dense <type> <n> <k> <bucket>
+ * <row_invariant> <bm> <bn> <splits>" line per dense plan and one "grouped <type> <n> <k> <experts>
+ * <bucket> <bm> <bn>" line per grouped plan to path (through path.tmp and a rename). */
 jk_status jk_tuner_save(const jk_tuner *t);
 
 #ifdef __cplusplus

@@ -104,6 +104,9 @@ SIGNATURES = {
     "jk_tuner_plan": (I, [P, P, S, I, ctypes.POINTER(Plan)]),
     "jk_tuner_tune": (I, [P, ctypes.POINTER(P), S, S, I, P, I, S, P, S, P, P, ctypes.POINTER(Plan)]),
     "jk_tuner_save": (I, [P]),
+    "jk_tuner_group_plan": (I, [P, P, S, ctypes.POINTER(Plan)]),
+    "jk_tuner_tune_grouped": (I, [P, ctypes.POINTER(P), S, S, S, P, S, P, I, S, P, S, P, P, P, S, P, P,
+                                  ctypes.POINTER(Plan)]),
 }
 
 STATUS = {0: "JK_OK", 1: "JK_ERR_INVALID", 2: "JK_ERR_UNSUPPORTED", 3: "JK_ERR_SHAPE", 4: "JK_ERR_CUDA",

@@ -1,9 +1,9 @@
-"""Measured launch plans for the dense products -- the reference's Tuner over libjk.so.
+"""Measured launch plans for the dense and grouped products -- the reference's Tuner over libjk.so.
 
 Mirrors crates/jevons-gemma4-diffusion/src/gpu/tune.rs: `bucket` (:74-76), `pick` (:548-562),
-`Tuner.new` / `dense` / `tune_dense` / `save` (:139-175, 231-269, 412-446). Candidate plans are
-timed on the device with CUDA events; row-invariant requests only consider plans without
-split-K, so tuning never changes a result a caller relies on being exact.
+`Tuner.new` / `dense` / `grouped` / `tune_dense` / `tune_grouped` / `save` (:139-192, 231-346,
+412-446). Candidate plans are timed on the device with CUDA events; row-invariant requests only
+consider plans without split-K, so tuning never changes a result a caller relies on being exact.
 """
 from __future__ import annotations
 
@@ -65,6 +65,37 @@ class Tuner:
         check(load().jk_tuner_tune(self._h, arr, len(ws), int(m), int(bool(row_invariant)), x.ptr(), x.dtype_code(),
                                    x.len(), out.ptr(), out.len(), scratch.handle if scratch else None, _stream(),
                                    ctypes.byref(chosen)))
+        return chosen
+
+    def grouped(self, w: QMatrix, rows: int) -> Plan:
+        """The grouped tile {bm, bn, 1} for w and bucket(rows), else {32, 128} (tune.rs:177-192)."""
+        out = Plan()
+        check(load().jk_tuner_group_plan(self._h, w.handle, int(rows), ctypes.byref(out)))
+        return out
+
+    def tune_grouped(self, ws: list[QMatrix], m: int, top_k: int, x: Buf, out: Buf,
+                     scratch: SplitScratch | None = None, ids: Buf | None = None) -> Plan:
+        """Times the grouped tiles for m tokens routed top_k ways (tune.rs:271-346). Without `ids`
+        the reference's synthetic balanced routing is used: route i goes to expert
+        ((i // top_k) * 7 + (i % top_k) * 13) % experts."""
+        import torch
+        experts = ws[0].experts
+        a = bucket(m) * top_k
+        dev = x.tensor.device
+        if ids is None:
+            i = torch.arange(a, device=dev, dtype=torch.int64)
+            ids = Buf((((i // top_k) * 7 + (i % top_k) * 13) % experts).to(torch.int32))
+        mj = int(load().jk_group_max_jobs(a, experts, 32))
+        sorted_ = torch.empty(max(a, 1), dtype=torch.int32, device=dev)
+        offsets = torch.empty(experts + 1, dtype=torch.int32, device=dev)
+        jobs = torch.empty(1 + 2 * mj, dtype=torch.int32, device=dev)
+        arr = (ctypes.c_void_p * len(ws))(*[w.handle.value for w in ws])
+        chosen = Plan()
+        check(load().jk_tuner_tune_grouped(self._h, arr, len(ws), int(m), int(top_k), ids.ptr(), ids.len(), x.ptr(),
+                                           x.dtype_code(), x.len(), out.ptr(), out.len(),
+                                           ctypes.c_void_p(sorted_.data_ptr()), ctypes.c_void_p(offsets.data_ptr()),
+                                           ctypes.c_void_p(jobs.data_ptr()), jobs.numel(),
+                                           scratch.handle if scratch else None, _stream(), ctypes.byref(chosen)))
         return chosen
 
     def save(self) -> None:

@@ -91,3 +91,47 @@ def test_lookup_falls_back_to_the_heuristic_and_table_round_trips(gpu, tmp_path)
         f.write("v0 another device\n" + "\n".join(lines[1:]) + "\n")
     assert len(tune.Tuner(gpu, path)) == 0
     os.remove(path)
+
+
+@pytest.mark.gpu
+def test_grouped_tuning_picks_a_tile_that_computes_the_grouped_product(gpu, tmp_path):
+    import torch
+    from jevons_kernels import synth
+    from jevons_kernels.gemm import (Buf, Groups, QMatrix, SplitScratch, group_max_jobs, group_routes,
+                                     matmul_grouped)
+    from oracle import oracle
+    experts, n, k, m, top_k = 16, 256, 512, 48, 4
+    raw = synth.q4k_blocks(np.random.default_rng(12), experts * n, k)
+    ws = [QMatrix.upload(gpu, oracle.Q4_K, n, k, experts, raw) for _ in range(2)]
+    a = tune.bucket(m) * top_k
+    x = torch.from_numpy(synth.activations(np.random.default_rng(13), a, k)).cuda().bfloat16()
+    out = torch.empty(a * n, device="cuda")
+    path = str(tmp_path / "autotune.txt")
+    t = tune.Tuner(gpu, path)
+    assert t.grouped(ws[0], m) == Plan(32, 128, 1)
+    chosen = t.tune_grouped(ws, m, top_k, Buf(x), Buf(out), SplitScratch(gpu))
+    assert t.grouped(ws[0], m) == chosen and chosen.splits == 1 and n % chosen.bn == 0
+    t.save()
+    assert f"grouped 12 {n} {k} {experts} {tune.bucket(m)} {chosen.bm} {chosen.bn}" in open(path).read()
+    assert tune.Tuner(gpu, path).grouped(ws[0], m) == chosen
+    # the chosen tile computes the grouped product of the reference's synthetic routes
+    ids = (np.arange(a) // top_k * 7 + np.arange(a) % top_k * 13) % experts
+    ids_t = torch.from_numpy(ids.astype(np.int32)).cuda()
+    mj = group_max_jobs(a, experts, chosen.bm)
+    sorted_ = torch.empty(a, dtype=torch.int32, device="cuda")
+    offsets = torch.empty(experts + 1, dtype=torch.int32, device="cuda")
+    jobs = torch.empty(1 + 2 * mj, dtype=torch.int32, device="cuda")
+    group_routes(gpu, Buf(ids_t), Buf(sorted_), Buf(offsets), Buf(jobs), a, experts, chosen.bm)
+    g = Groups(Buf(sorted_), Buf(offsets), Buf(jobs), mj, 1, a)
+    res = torch.empty(a, n, device="cuda")
+    matmul_grouped(gpu, Buf(x), ws[0], g, Buf(res), chosen.bm, chosen.bn, 1, SplitScratch(gpu))
+    torch.cuda.synchronize()
+    dense = oracle.dequantize(oracle.Q4_K, raw).reshape(experts * n, k)
+    xe = x.float().cpu().numpy()
+    want = oracle.matmul_grouped_f64(xe, dense, n, ids, 1)
+    # the product bound of every GPU test, per route with its own expert's rows:
+    # |err[r, c]| <= 1e-3 |x_r| |W_ids[r], c|
+    wn = oracle.row_norms(dense).reshape(experts, n)
+    bound = 1e-3 * oracle.row_norms(xe)[:, None] * wn[ids]
+    assert np.all(np.abs(res.cpu().numpy() - want) <= bound)
+    assert gpu.device_error() == 0

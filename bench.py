@@ -16,11 +16,13 @@ layer's f32 output shard is all-gathered over NVLink (torch.distributed / NCCL) 
 stream, overlapped with the next layer's product.
 
 Printed JSON (rank 0): `value` = aggregate TFLOP/s of the timed steps (inputs resident in HBM,
-device-timed with CUDA events, max over ranks); `e2e` = the same through the public API with
-pinned host buffers (per step: activations host->device, the layer stack, the last layer's output
-device->host); `roofline` = the tensor-core kernel's achieved TFLOP/s per launch vs the measured
-bf16 peak; `gemv` = the M=1 weight-streaming GB/s on the same matrices; `cpu_baseline` = the
-reference's CPU arithmetic (quant.rs dequant restated in C + a CPU f32 matmul) on a bounded sample.
+device-timed with CUDA events, max over ranks); `e2e` = the same metric through the public API with
+pinned host buffers, one product per step (its activations host->device, the product, its whole
+f32 output device->host); `roofline` = the tensor-core kernel's achieved TFLOP/s per launch vs the
+measured bf16 burst peak; `f16` = the same stack with FP16 activations; `gemv` = the M=1
+weight-streaming GB/s on the same matrices and `gemv_vocab` on config 4's 377 MB matrix;
+`cpu_baseline` = the reference's CPU arithmetic (quant.rs dequant restated in C + a CPU f32
+matmul) on a bounded sample.
 """
 from __future__ import annotations
 
@@ -40,6 +42,7 @@ for p in (os.path.join(REPO, "jevons-rs_b200"), REPO):
 import numpy as np  # noqa: E402
 
 K_DIM, N_DIM, M_ROWS, LAYERS = 2560, 10240, 256, 36
+VOCAB_N = 262144  # config 4's vocabulary: the M=1 product over its head matrix
 METRIC = "Q4_K GEMM TFLOP/s (M=256)"
 WORKLOAD = "q4k_ffn_up_m256"
 Q4_K = 12
@@ -489,7 +492,9 @@ def run_ours(args):
     # partials in-kernel), so its average duration is the step time over the layers.
     per_launch_ms = ms / args.steps / L
     pk, pk_kind = peaks()
-    peak = pk.get("bf16_tflops_sustained", pk.get("bf16_tflops"))
+    # The timed region is steps x ~1 ms (tens of ms, not a seconds-long power-capped loop), so the
+    # kernel is rated against the burst bf16 figure.
+    peak = pk.get("bf16_tflops", pk.get("bf16_tflops_sustained"))
     achieved = 2.0 * M_ROWS * N_DIM * K_DIM / (per_launch_ms * 1e-3) / 1e12
     traffic = None
     try:
@@ -524,18 +529,61 @@ def run_ours(args):
     m32_tflops = 2.0 * 32 * N_DIM * K_DIM * L * gv_steps * world / (c_ms * 1e-3) / 1e12
 
     # ---- e2e: host buffers through the public API -------------------------------------------
+    # One step = one product as a caller runs it: the step's activations host->device from pinned
+    # memory, the product (jk_matmul), and its whole f32 output device->host. Steps rotate over
+    # the L distinct matrices, so the weights stream from HBM as in the device-timed step.
+    # With N GPUs the step's result is the all-gathered [N, M, N_DIM] output, read back whole.
     xh = x.cpu().pin_memory()
-    oh = torch.empty(M_ROWS, N_DIM, dtype=torch.float32).pin_memory()
+    oh = torch.empty(world, M_ROWS, N_DIM, dtype=torch.float32).pin_memory()
     xd = torch.empty_like(x)
     xdb = Buf(xd)
+    e2e_state = {"i": 0}
 
-    def e2e_step():
+    def e2e_product():
+        i = e2e_state["i"]
+        e2e_state["i"] = (i + 1) % L
         xd.copy_(xh, non_blocking=True)
-        step(xdb)
-        oh.copy_(outs[L - 1], non_blocking=True)
+        matmul(gpu, xdb, M_ROWS, ws[i], obufs[i], None, scratch)
+        if world > 1:
+            gather_shards(outs[i], out=gathered[i])
+            oh.copy_(gathered[i], non_blocking=True)
+        else:
+            oh[0].copy_(outs[i], non_blocking=True)
 
-    e_ms = timed(e2e_step, args.steps, args.warmup)
-    e2e_value = flops_step * world * args.steps / (e_ms * 1e-3) / 1e12
+    e_steps = max(args.steps, 2 * L)
+    e_ms = timed(e2e_product, e_steps, args.warmup, use_graph=False)
+    e2e_value = 2.0 * M_ROWS * N_DIM * K_DIM * world * e_steps / (e_ms * 1e-3) / 1e12
+    e2e_d2h = oh.numel() * 4
+
+    # ---- the same stack at the reference's operand precision (FP16 activations) -------------
+    x16 = x.float().half()
+    x16b = Buf(x16)
+
+    def step16():
+        for i in range(L):
+            matmul(gpu, x16b, M_ROWS, ws[i], obufs[i], None, scratch)
+    f16_ms = timed(step16, args.steps, args.warmup)
+    f16_tflops = flops_step * world * args.steps / (f16_ms * 1e-3) / 1e12
+
+    # ---- GEMV at config 4's K, N (M=1 over a 377 MB Q4_K matrix, larger than L2) --------------
+    gv4 = None
+    if not args.no_vocab_gemv:
+        raw4 = synth.q4k_blocks(np.random.default_rng(40 + rank), VOCAB_N, K_DIM)
+        w4 = QMatrix.upload(gpu, Q4_K, VOCAB_N, K_DIM, 1, raw4)
+        del raw4
+        o4 = torch.empty(1, VOCAB_N, device=dev)
+        o4b = Buf(o4)
+
+        def gemv4():
+            matvec(gpu, x1b, 1, w4, o4b)
+        g4_steps = 20
+        g4_ms = timed(gemv4, g4_steps, 3)
+        wb4 = VOCAB_N * K_DIM // 256 * 144
+        gv4 = {"metric": "Q4_K GEMV weight-GB/s (M=1, K=2560, N=262144: config 4's matrix, 377 MB > L2)",
+               "value": wb4 * g4_steps / (g4_ms * 1e-3) / 1e9, "unit": "GB/s",
+               "frac_of_hbm": wb4 * g4_steps / (g4_ms * 1e-3) / 1e9 / pk.get("hbm_gbs", 1.0),
+               "us_per_product": g4_ms / g4_steps * 1e3}
+        del w4
 
     # ---- expert-grouped products (the reference's routed workloads), one GPU only -------------
     grouped = None
@@ -566,7 +614,7 @@ def run_ours(args):
                          "frac": achieved / peak, "traffic": traffic,
                          "kernel": f"gemm_tc_kernel<Q4_K,bf16,{plan.bm}>",
                          "per_launch_ms": per_launch_ms,
-                         "peak_source": f"{pk_kind} bf16_tflops_sustained (kernel timed inside a long step)"},
+                         "peak_source": f"{pk_kind} bf16_tflops (burst: the timed region is {ms:.0f} ms)"},
             "gemv": {"metric": "Q4_K GEMV weight-GB/s (M=1)", "value": gemv_gbs, "unit": "GB/s",
                      "peak_hbm_gbs": pk.get("hbm_gbs"), "frac_of_hbm": gemv_gbs / pk.get("hbm_gbs", 1.0),
                      "algorithmic_gbs": gemv_gbs * alg_bytes / wbytes, "ms_per_product": gv_ms / gv_steps / L},
@@ -575,7 +623,12 @@ def run_ours(args):
             "grouped": grouped,
             "head": head_ops,
             "e2e": {"value": e2e_value, "unit": "TFLOP/s", "h2d_bytes_per_step": xh.numel() * 2,
-                    "d2h_bytes_per_step": oh.numel() * 4},
+                    "d2h_bytes_per_step": e2e_d2h, "steps": e_steps,
+                    "what": "per step: x host->device (pinned), one jk_matmul product, its whole f32 output "
+                            "device->host; steps rotate over the distinct matrices; CUDA events"},
+            "f16": {"metric": "Q4_K GEMM TFLOP/s (M=256), FP16 activations (the reference's operand type)",
+                    "value": f16_tflops, "unit": "TFLOP/s", "ms_per_step": f16_ms / args.steps},
+            "gemv_vocab": gv4,
             "gpu_launches": args.steps * L * launches_per_product,
             "timing": "CUDA graph replay of each step, CUDA events, max over ranks",
             "clocks": sampler.report(),
@@ -599,6 +652,7 @@ def main():
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--no-grouped", action="store_true", help="skip the expert-grouped workloads")
     ap.add_argument("--no-head", action="store_true", help="skip the Q6_K embedding-table workloads")
+    ap.add_argument("--no-vocab-gemv", action="store_true", help="skip the M=1 product over config 4's matrix")
     ap.add_argument("--head-only", action="store_true", help="run only the Q6_K embedding-table workloads")
     ap.add_argument("--head-vocab", type=int, default=HEAD_VOCAB, help="table rows of the head workloads")
     args = ap.parse_args()

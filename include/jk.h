@@ -85,6 +85,13 @@ jk_status jk_pack(int type, const void *ggml_bytes, size_t len,
                   uint32_t *q, size_t q_words, uint32_t *h, size_t h_words,
                   uint32_t *s, size_t s_words, float *d, size_t d_words);
 
+/* quant::dequantize (quant.rs:83-101), on the host: decodes `len` bytes of whole blocks of `type`
+ * (F32, F16, Q4_K, Q6_K, Q5_0, Q8_0) into out[out_len] f32, bit-exact with the reference (the same
+ * f32 operations in the same order). JK_ERR_UNSUPPORTED "unsupported tensor type" for other ids;
+ * JK_ERR_SHAPE "dequantization size mismatch" unless len is a whole number of blocks and out_len
+ * is exactly blocks * elements per block. The device counterpart is jk_qmatrix_dequantize. */
+jk_status jk_dequantize(int type, const void *bytes, size_t len, float *out, size_t out_len);
+
 /* ---- device ------------------------------------------------------------------------------- */
 
 /* Gpu::new (crates/jevons-kernels/src/lib.rs:181-191): checks that `device` exists and is a
@@ -200,6 +207,14 @@ jk_status jk_matmul_tiled(const jk_qmatrix *w, const void *x, int x_dtype, size_
 jk_status jk_f16_linear(const void *x_f16, size_t m, size_t k, const void *w_f16, size_t n,
                         float *out, void *stream);
 
+/* jevons_burn::kernels::f16_linear_scaled (kernels.rs:116-129): jk_f16_linear for f32 activations
+ * of any magnitude. Row r of x is divided by s_r = max(max_j |x[r, j]| / 16384, 1) (f32 division)
+ * and cast to FP16, the FP16 product runs, and out[r, :] is multiplied back by s_r (rows with
+ * s_r == 1 give exactly jk_f16_linear of the FP16-cast row). The FP16 rows and scales live in
+ * `scratch` (required; grown like jk_matmul_plan's). */
+jk_status jk_f16_linear_scaled(const float *x_f32, size_t m, size_t k, const void *w_f16, size_t n,
+                               float *out, jk_split_scratch *scratch, void *stream);
+
 /* ---- expert-grouped products ----------------------------------------------------------------- */
 
 /* Groups (gemm.rs:955-966): a device-side grouping of routed rows by expert, as written by
@@ -256,8 +271,8 @@ jk_status jk_matvec_grouped(const jk_qmatrix *w, const void *x, int x_dtype, siz
 
 /* No counterpart in the reference: an addition for callers that cannot allocate device memory
  * while they run a product -- code under a framework that owns every device allocation (a
- * cudaMalloc from the library would escape its accounting or exceed its cap), code inside a
- * stream capture, or paths where the device synchronisation of a cudaMalloc is not acceptable.
+ * cudaMalloc from the library would escape its accounting or exceed its cap), or paths where the
+ * device synchronisation of a cudaMalloc is not acceptable.
  * Computes the same product as jk_matmul_plan with plan {bm, 128, splits > 1} (the stream-K
  * schedule), with its scratch in a fixed buffer inside the library instead of a jk_split_scratch;
  * it calls no cudaMalloc, cudaFree or allocating routine. Activations must be bf16 or f16

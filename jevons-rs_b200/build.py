@@ -25,7 +25,7 @@ INCLUDE = os.path.join(REPO, "include")
 
 ARCH = ["-gencode", "arch=compute_100a,code=sm_100a"]
 NVCC_FLAGS = ARCH + [
-    "-O3", "-lineinfo", "-std=c++17", "-Xcompiler", "-fPIC", "-Xcompiler", "-Wall",
+    "-O3", "-lineinfo", "-std=c++17", "-Xcompiler", "-fPIC", "-Xcompiler", "-Wall", "-Xcompiler", "-ffp-contract=off",
     "--expt-relaxed-constexpr", "-I", CSRC, "-I", INCLUDE,
 ]
 

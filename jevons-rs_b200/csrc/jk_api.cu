@@ -331,6 +331,95 @@ extern "C" jk_status jk_pack(int type, const void* ggml_bytes, size_t len, uint3
     return JK_OK;
 }
 
+// Host dequantization of whole blocks, quant::dequantize (crates/jevons-formats/src/quant.rs:83-101)
+// with the block decoders of quant.rs:25-80. Every product of a scale and a quant is exact in f32
+// (d has 11 significant bits, the other factor at most 13), so the only rounding is Q4_K's final
+// subtraction; the operations below keep the reference's order (the library is compiled with
+// -ffp-contract=off, so the multiply and the subtraction stay two operations).
+namespace {
+
+void host_block_q4k(const uint8_t* b, float* out) {
+    const float d = half_to_float(le16(b)), dmin = half_to_float(le16(b + 2));
+    const uint8_t* sc = b + 4;
+    const uint8_t* qs = b + 16;
+    for (int pair = 0; pair < 4; ++pair) {
+        float dd[2], mm[2];
+        for (int h = 0; h < 2; ++h) {
+            uint8_t s, m;
+            jk_q4k_scale_min(2 * pair + h, sc, &s, &m);
+            dd[h] = d * (float)s;
+            mm[h] = dmin * (float)m;
+        }
+        for (int l = 0; l < 32; ++l) {
+            const uint8_t q = qs[32 * pair + l];
+            const float lo = dd[0] * (float)(q & 15), hi = dd[1] * (float)(q >> 4);
+            out[64 * pair + l] = lo - mm[0];
+            out[64 * pair + 32 + l] = hi - mm[1];
+        }
+    }
+}
+
+void host_block_q6k(const uint8_t* b, float* out) {
+    const float d = half_to_float(le16(b + 208));
+    for (int h = 0; h < 2; ++h) {
+        const uint8_t* ql = b + 64 * h;
+        const uint8_t* qh = b + 128 + 32 * h;
+        const int8_t* sc = reinterpret_cast<const int8_t*>(b + 192 + 8 * h);
+        float* o = out + 128 * h;
+        for (int l = 0; l < 32; ++l) {
+            const int is = l / 16;
+            const int q[4] = {((ql[l] & 15) | ((qh[l] & 3) << 4)) - 32, ((ql[l + 32] & 15) | (((qh[l] >> 2) & 3) << 4)) - 32,
+                              ((ql[l] >> 4) | (((qh[l] >> 4) & 3) << 4)) - 32,
+                              ((ql[l + 32] >> 4) | (((qh[l] >> 6) & 3) << 4)) - 32};
+            for (int j = 0; j < 4; ++j) {
+                const float ds = d * (float)sc[is + 2 * j];
+                o[l + 32 * j] = ds * (float)q[j];
+            }
+        }
+    }
+}
+
+void host_block_q5_0(const uint8_t* b, float* out) {
+    const float d = half_to_float(le16(b));
+    const uint32_t qh = le32(b + 2);
+    const uint8_t* qs = b + 6;
+    for (int j = 0; j < 16; ++j) {
+        const uint32_t h0 = ((qh >> j) << 4) & 0x10u, h1 = (qh >> (j + 12)) & 0x10u;
+        out[j] = d * (float)((int)((qs[j] & 15u) | h0) - 16);
+        out[j + 16] = d * (float)((int)((qs[j] >> 4) | h1) - 16);
+    }
+}
+
+void host_block_q8_0(const uint8_t* b, float* out) {
+    const float d = half_to_float(le16(b));
+    for (int j = 0; j < 32; ++j) out[j] = d * (float)(int8_t)b[2 + j];
+}
+
+}  // namespace
+
+extern "C" jk_status jk_dequantize(int type, const void* bytes, size_t len, float* out, size_t out_len) {
+    uint64_t be, bb;
+    if (!block_of(type, be, bb)) return fail(JK_ERR_UNSUPPORTED, "unsupported tensor type");
+    if (len % bb || out_len != len / bb * be) return fail(JK_ERR_SHAPE, "dequantization size mismatch");
+    if (len && (!bytes || !out)) return fail(JK_ERR_INVALID, "null pointer");
+    const uint8_t* raw = static_cast<const uint8_t*>(bytes);
+    parallel_for(len / bb, [&](size_t b0, size_t b1) {
+        for (size_t i = b0; i < b1; ++i) {
+            const uint8_t* src = raw + i * bb;
+            float* dst = out + i * be;
+            switch (type) {
+            case JK_TYPE_F32: memcpy(dst, src, 4); break;
+            case JK_TYPE_F16: dst[0] = half_to_float(le16(src)); break;
+            case JK_TYPE_Q4_K: host_block_q4k(src, dst); break;
+            case JK_TYPE_Q6_K: host_block_q6k(src, dst); break;
+            case JK_TYPE_Q5_0: host_block_q5_0(src, dst); break;
+            default: host_block_q8_0(src, dst); break;
+            }
+        }
+    });
+    return JK_OK;
+}
+
 // ================================================================================================
 // device
 // ================================================================================================
@@ -649,6 +738,8 @@ jk_status check_launch(const jk_qmatrix* w, const void* x, int x_dtype, size_t x
     if (!w) return fail(JK_ERR_INVALID, "null matrix");
     if (x_dtype != JK_DTYPE_F32 && x_dtype != JK_DTYPE_F16 && x_dtype != JK_DTYPE_BF16)
         return fail(JK_ERR_INVALID, "unknown activation dtype");
+    // m is bounded first so that m * k and m * n below cannot wrap around
+    if (m > (size_t)INT32_MAX) return fail(JK_ERR_INVALID, "m too large");
     if (x_len < m * w->k || out_len < m * w->n) {
         char buf[200];
         snprintf(buf, sizeof buf, "%s: buffers too small for m=%zu (x %zu < %zu or out %zu < %zu)",
@@ -723,7 +814,7 @@ extern "C" void jk_split_scratch_destroy(jk_split_scratch* s) {
 
 // Grows the scratch to `bytes` (cudaMalloc, synchronising the device) and zeroes it, so the
 // stream-K flag words at its start begin at zero.
-static jk_status scratch_get(jk_split_scratch* s, size_t bytes, void** out) {
+jk_status jk::scratch_reserve(jk_split_scratch* s, size_t bytes, void** out) {
     if (s->bytes < bytes) {
         DeviceGuard g(s->device);
         if (s->buf) {
@@ -789,7 +880,7 @@ extern "C" jk_status jk_matmul_plan(const jk_qmatrix* w, const void* x, int x_dt
     if (ws_bytes + conv_bytes) {
         if (!scratch) return fail(JK_ERR_INVALID, "this plan needs a split-K scratch (splits > 1 or f32 activations)");
         if (scratch->device != w->device) return fail(JK_ERR_INVALID, "scratch belongs to another device");
-        st = scratch_get(scratch, ws_bytes + conv_bytes, &sbuf);
+        st = jk::scratch_reserve(scratch, ws_bytes + conv_bytes, &sbuf);
         if (st != JK_OK) return st;
     }
     const void* xk = x;
@@ -888,7 +979,7 @@ extern "C" jk_status jk_matmul_grouped(const jk_qmatrix* w, const void* x, int x
     // expect to find zero
     const size_t flags = jk::stream_k_flag_bytes(w->device);
     void* sbuf = nullptr;
-    st = scratch_get(scratch, flags + (g->rows * w->k * 2 + 255) / 256 * 256, &sbuf);
+    st = jk::scratch_reserve(scratch, flags + (g->rows * w->k * 2 + 255) / 256 * 256, &sbuf);
     if (st != JK_OK) return st;
     void* xs = static_cast<char*>(sbuf) + flags;
     st = jk::launch_gather_rows(x, x_dtype, x_rows, w->k, g->sorted, g->rows, g->in_div, xs, want_bf16, cs);

@@ -51,6 +51,10 @@ jk_status cuda_fail(cudaError_t e, const char* what);
 // Per-device error word (a __device__ variable; no allocation).
 uint32_t* device_error_word(int device);
 
+// Grows a split scratch to at least `bytes` (cudaMalloc + zeroing on growth, which synchronise the
+// device) and returns its base; the first stream_k_flag_bytes() stay zero between products.
+jk_status scratch_reserve(jk_split_scratch* s, size_t bytes, void** out);
+
 // Multiprocessor count of `device` (cached).
 int sm_count(int device);
 // SMs the products may occupy on `device`: sm_count, or the jk_set_max_ctas cap when smaller.

@@ -1,12 +1,13 @@
 // jk_noalloc.cu -- the allocation-free stream-K product (jk_matmul_splitk_noalloc).
 //
 // Some callers cannot allocate device memory at the time they run a product: code that runs
-// under a host allocator or pool it does not control (a framework that owns every cudaMalloc on
-// the device, so a library allocation would bypass its accounting or fail under its memory cap),
-// code inside a CUDA stream capture (cudaMalloc is not capturable), and latency-critical paths
-// where a cudaMalloc -- which synchronises the device -- is not acceptable. For them this entry
-// point runs the split-K (stream-K) tensor-core product with its scratch in a fixed buffer that
-// the library itself declares below; it calls no cudaMalloc, cudaFree or allocating routine.
+// under an allocator or pool it does not control (a framework that owns every cudaMalloc on the
+// device, so a library allocation would bypass its accounting or fail under its memory cap), and
+// latency-critical paths where a cudaMalloc -- which synchronises the device -- is not
+// acceptable. For them this entry point runs the split-K (stream-K) tensor-core product with its
+// scratch in a fixed buffer that the library itself declares below; it calls no cudaMalloc,
+// cudaFree or allocating routine. Its first call on a device looks up the buffer's device address
+// (cudaGetSymbolAddress, no allocation): make that first call before any stream capture.
 //
 // The buffer is a file-scope __device__ array: every GPU that loads libjk.so holds
 // JK_NOALLOC_SCRATCH_BYTES (20 MiB) of device memory for it until the process exits. Its layout:
@@ -63,6 +64,8 @@ extern "C" jk_status jk_matmul_splitk_noalloc(const jk_qmatrix* w, const void* x
                         "the allocation-free product takes bf16 or f16 activations (f32 would need a conversion buffer)");
     if (w->type == JK_TYPE_F16 && x_dtype != JK_DTYPE_F16)
         return jk::fail(JK_ERR_UNSUPPORTED, "FP16 weights need FP16 activations");
+    // m is bounded first so that m * k and m * n below cannot wrap around
+    if (m > (size_t)INT32_MAX) return jk::fail(JK_ERR_INVALID, "m too large");
     if (x_len < m * w->k || out_len < m * w->n) {
         char buf[160];
         snprintf(buf, sizeof buf, "buffers too small for m=%zu (x %zu < %zu or out %zu < %zu)", m, x_len, m * w->k,
@@ -72,7 +75,6 @@ extern "C" jk_status jk_matmul_splitk_noalloc(const jk_qmatrix* w, const void* x
     if (m == 0) return JK_OK;
     if (!x || !out) return jk::fail(JK_ERR_INVALID, "null activation or output pointer");
     if ((reinterpret_cast<uintptr_t>(x) & 15) != 0) return jk::fail(JK_ERR_INVALID, "activations must be 16-byte aligned");
-    if (m > (size_t)INT32_MAX) return jk::fail(JK_ERR_INVALID, "m too large");
 
     int prev = -1;
     cudaGetDevice(&prev);

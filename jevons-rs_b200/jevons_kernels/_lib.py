@@ -70,6 +70,8 @@ SIGNATURES = {
     "jk_matvec": (I, [P, P, I, S, S, P, S, P]),
     "jk_matmul_tiled": (I, [P, P, I, S, S, P, S, I, I, P]),
     "jk_f16_linear": (I, [P, S, S, P, S, P, P]),
+    "jk_f16_linear_scaled": (I, [P, S, S, P, S, P, P, P]),
+    "jk_dequantize": (I, [I, P, S, P, S]),
     "jk_matmul_splitk_noalloc": (I, [P, P, I, S, S, P, S, I, P]),
     "jk_set_max_ctas": (I, [I, I]),
     "jk_get_max_ctas": (I, [I, ctypes.POINTER(I), ctypes.POINTER(I)]),

@@ -1,7 +1,8 @@
 """GGML block types and host-side repacking -- the `jevons-formats` items the matmul path uses.
 
 Mirrors crates/jevons-formats/src/gguf.rs:109-145 (`TensorType`, `block()`) and
-crates/jevons-formats/src/quant.rs:13-193 (`q4k_scale_min`, `Packed`, `packed_words`, `pack`).
+crates/jevons-formats/src/quant.rs:13-193 (`q4k_scale_min`, `dequantize`, `Packed`, `packed_words`,
+`pack`).
 All work happens in libjk.so; this module only marshals arguments.
 """
 from __future__ import annotations
@@ -82,3 +83,16 @@ def pack(kind, raw) -> Packed:
     check(load().jk_pack(int(kind), raw.ctypes.data_as(ctypes.c_void_p), raw.size, _ptr(q), q.size, _ptr(h),
                          h.size, _ptr(s), s.size, _ptr(d), d.size))
     return Packed(q, h, s, d)
+
+
+def dequantize(kind, raw) -> np.ndarray:
+    """quant.rs:83-101 on the host (jk_dequantize): whole blocks of `kind` -> f32, bit-exact."""
+    raw = np.ascontiguousarray(np.frombuffer(raw, dtype=np.uint8) if isinstance(raw, (bytes, bytearray))
+                               else np.asarray(raw).view(np.uint8).reshape(-1))
+    bk = block(int(kind))
+    if bk is None:  # raises JK_ERR_UNSUPPORTED "unsupported tensor type"
+        check(load().jk_dequantize(int(kind), None, 0, None, 0))
+    elems, size = bk
+    out = np.empty(raw.size // size * elems if raw.size % size == 0 else 0, np.float32)
+    check(load().jk_dequantize(int(kind), _ptr(raw), raw.size, _ptr(out), out.size))
+    return out

@@ -355,13 +355,27 @@ def f16_linear(x: torch.Tensor, weight: torch.Tensor) -> torch.Tensor:
 
 
 F16_ROW_LIMIT = 16384.0  # kernels.rs:105
+_SCALED_SCRATCH: dict = {}
 
 
 def f16_linear_scaled(x: torch.Tensor, weight: torch.Tensor) -> torch.Tensor:
-    """kernels.rs:116-129: rows with max |x| > 16384 are divided down first and scaled back."""
-    x = x.float()
-    scale = (x.abs().amax(dim=1, keepdim=True) / F16_ROW_LIMIT).clamp_min(1.0)
-    return f16_linear(x / scale, weight) * scale
+    """kernels.rs:116-129 (jk_f16_linear_scaled): rows with max |x| > 16384 are divided down by
+    max / 16384 before the FP16 cast and their outputs multiplied back; other rows use exactly 1."""
+    if weight.dtype != torch.float16:
+        raise JkError(1, "f16 matmul needs FP16 operands")
+    x32 = x.float().contiguous()
+    w = weight.contiguous()
+    m, k = x32.shape
+    n = w.shape[0]
+    if w.shape[1] != k:
+        raise JkError(1, "f16 matmul needs dense row-major [M, K] x [N, K]")
+    dev = x32.device.index if x32.device.index is not None else torch.cuda.current_device()
+    if dev not in _SCALED_SCRATCH:
+        _SCALED_SCRATCH[dev] = SplitScratch(Gpu(dev))
+    out = torch.empty(m, n, dtype=torch.float32, device=x32.device)
+    check(load().jk_f16_linear_scaled(ctypes.c_void_p(x32.data_ptr()), m, k, ctypes.c_void_p(w.data_ptr()), n,
+                                      ctypes.c_void_p(out.data_ptr()), _SCALED_SCRATCH[dev].handle, _stream()))
+    return out
 
 
 __all__ = ["GEMV_ROWS", "Gpu", "Buf", "QMatrix", "Plan", "SplitScratch", "matmul", "matmul_plan", "matmul_tiled",

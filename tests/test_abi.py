@@ -117,3 +117,59 @@ def test_head_operators_reject_null_arguments_without_a_device():
     assert lib.jk_softcap(null, 4, ctypes.c_float(30.0), null) == 1
     assert "softcap" in lib.jk_last_error().decode()
     assert lib.jk_softcap(null, 0, ctypes.c_float(30.0), null) == 0  # nothing to do
+
+
+# --- host dequantization: quant::dequantize (crates/jevons-formats/src/quant.rs:83-101) -------------
+
+def host_dequantize(kind, raw, out_len=None):
+    raw = np.ascontiguousarray(np.frombuffer(bytes(raw), np.uint8)) if not isinstance(raw, np.ndarray) else raw
+    if out_len is None:
+        elems, size = {0: (1, 4), 1: (1, 2), 12: (256, 144), 14: (256, 210), 6: (32, 22), 8: (32, 34)}[kind]
+        out_len = len(raw) // size * elems
+    out = np.full(max(out_len, 1), np.nan, np.float32)
+    st = load().jk_dequantize(kind, raw.ctypes.data_as(ctypes.c_void_p) if len(raw) else None, len(raw),
+                              out.ctypes.data_as(ctypes.c_void_p), out_len)
+    return st, out[:out_len]
+
+
+@pytest.mark.parametrize("name", ["Q4_K", "Q6_K", "Q8_0", "Q5_0"])
+def test_host_dequantize_is_bit_exact_with_the_oracle(name):
+    from oracle import oracle
+    from jevons_kernels import synth
+    kind = {"Q4_K": oracle.Q4_K, "Q6_K": oracle.Q6_K, "Q8_0": oracle.Q8_0, "Q5_0": oracle.Q5_0}[name]
+    raw = synth.weights(kind, np.random.default_rng(5), 320, 1024)
+    st, got = host_dequantize(kind, raw)
+    assert st == 0
+    want = oracle.dequantize(kind, raw)
+    assert np.array_equal(got.view(np.uint32), want.view(np.uint32))
+    # arbitrary bytes: NaN / inf / subnormal scales and every quant pattern
+    junk = np.random.default_rng(6).integers(0, 256, size=len(raw), dtype=np.uint8)
+    st, got = host_dequantize(kind, junk)
+    want = oracle.dequantize(kind, junk)
+    assert st == 0
+    same = (got.view(np.uint32) == want.view(np.uint32)) | (np.isnan(got) & np.isnan(want))
+    assert same.all()
+
+
+def test_host_dequantize_reference_known_answers():
+    """The reference's own dequantization KATs (quant.rs:210-225), kept in tests/golden."""
+    import json
+    kat = json.load(open(os.path.join(REPO, "tests", "golden", "quant_kat.json")))
+    for case in ("q8_0", "q5_0"):
+        st, out = host_dequantize(kat[case]["type"], bytes(kat[case]["bytes"]))
+        assert st == 0
+        for i, v in kat[case]["expect"].items():
+            assert out[int(i)] == v, (case, i)
+
+
+def test_host_dequantize_errors_follow_the_reference():
+    st, _ = host_dequantize(8, bytes(33), 32)
+    assert st == 3 and load().jk_last_error().decode() == "dequantization size mismatch"
+    st, _ = host_dequantize(8, bytes(34), 31)
+    assert st == 3
+    st, _ = host_dequantize(2, bytes(18), 32)
+    assert st == 2 and load().jk_last_error().decode() == "unsupported tensor type"
+    st, out = host_dequantize(1, np.float16([1.5, -2.0]).view(np.uint8).copy())
+    assert st == 0 and list(out) == [1.5, -2.0]
+    st, out = host_dequantize(0, np.float32([3.25]).view(np.uint8).copy())
+    assert st == 0 and out[0] == 3.25

@@ -166,15 +166,21 @@ def test_f16_outputs_beyond_the_fp16_range_stay_exact(gpu):
 
 
 def test_f16_linear_scaled_handles_huge_rows(gpu):
-    from jevons_kernels.gemm import f16_linear_scaled
+    """jk_f16_linear_scaled (kernels.rs:116-129): a row far beyond the FP16 range is scaled down and
+    back; rows within it give exactly the f16_linear product of the FP16-cast row."""
+    from jevons_kernels.gemm import f16_linear, f16_linear_scaled
     m, n, k = 32, 128, 256
     x = torch.randn(m, k, device="cuda")
     x[3] *= 1e6
+    x[7] *= 3e4  # just above the 16384 limit
     w = (torch.randn(n, k, device="cuda") * 0.05).half()
-    want = x @ w.float().t()
+    want = x.double() @ w.double().t()
     got = f16_linear_scaled(x, w)
-    rel = ((want - got).abs().max(dim=1).values / want.abs().max(dim=1).values).max().item()
+    rel = ((want - got.double()).abs().max(dim=1).values / want.abs().max(dim=1).values).max().item()
     assert rel < 2e-3
+    plain = [r for r in range(m) if r not in (3, 7)]
+    ref = f16_linear(x[plain].contiguous(), w)
+    assert torch.equal(got[plain], ref)
 
 
 # --- BASELINE configurations -------------------------------------------------------------------
@@ -187,6 +193,52 @@ def test_config1_q4k_m32(gpu):
     out = torch.empty(32, 10240, device="cuda")
     matmul_plan(gpu, Buf(x), 32, w, Buf(out), None, None, Plan(32, 128, 1))
     assert_close("cfg1", out.cpu().numpy(), x_exact, dense)
+
+
+@pytest.mark.parametrize("dtype", [torch.bfloat16, torch.float16])
+def test_bench_headline_q4k_m256_full_size(gpu, dtype):
+    """The bench's timed workload exactly (Q4_K M=256, K=2560 -> N=10240, the bench's seeds) through
+    the public entry points: the whole-tile plan {128, 128, 1}, the CTA-pair plan {256, 256, 1} and
+    the heuristic plan, every output element against the f64 oracle."""
+    from jevons_kernels.gemm import Buf, Plan, QMatrix, SplitScratch, matmul, matmul_plan
+    n, k, m = 10240, 2560, 256
+    raw = synth.q4k_blocks(np.random.default_rng(1), n, k)
+    w = QMatrix.upload(gpu, oracle.Q4_K, n, k, 1, raw)
+    dense = oracle.dequantize(oracle.Q4_K, raw).reshape(n, k)
+    x = torch.from_numpy(synth.activations(np.random.default_rng(2), m, k)).cuda().to(dtype)
+    x_exact = x.float().cpu().numpy()
+    want = oracle.matmul_f64(x_exact, dense)
+    scratch = SplitScratch(gpu)
+    for plan in (Plan(128, 128, 1), Plan(256, 256, 1), Plan.heuristic(w, m, False), None):
+        out = torch.full((m, n), float("nan"), device="cuda")
+        if plan is None:
+            matmul(gpu, Buf(x), m, w, Buf(out), None, scratch)
+        else:
+            matmul_plan(gpu, Buf(x), m, w, Buf(out), None, scratch, plan)
+        assert_close(f"bench headline {plan} {dtype}", out.cpu().numpy(), x_exact, dense, want,
+                     ref_rule=dtype == torch.float16)
+    assert gpu.device_error() == 0
+
+
+# BASELINE config 3: FastConformer (Parakeet) encoder linears, Q8_0 weights, M=750 frames of f32
+# activations ~N(0, 1): FFN 1024 -> 4096 -> 1024 and four 1024 -> 1024 attention projections
+# (crates/jevons-parakeet/src/config.rs:183-186, encoder.rs:53-61).
+CONFIG3_SHAPES = [("ffn_up", 4096, 1024), ("ffn_down", 1024, 4096), ("attn_qkvo", 1024, 1024)]
+
+
+@pytest.mark.parametrize("name,n,k", CONFIG3_SHAPES)
+def test_config3_parakeet_q8_0_m750(gpu, name, n, k):
+    """Config 3 through jk_matmul (f32 activations are rounded to bf16 for the tensor cores, so the
+    oracle product uses the bf16-rounded rows) against the f64 oracle."""
+    from jevons_kernels.gemm import Buf, SplitScratch, matmul
+    m = 750
+    w, _, dense = make_weights(gpu, KINDS["Q8_0"], n, k, seed=300 + n + k)
+    x, x_exact = activations(m, k, torch.float32, seed=3)
+    x_exact = synth.bf16_round(x_exact)
+    out = torch.full((m, n), float("nan"), device="cuda")
+    matmul(gpu, Buf(x), m, w, Buf(out), None, SplitScratch(gpu))
+    assert_close(f"cfg3 {name}", out.cpu().numpy(), x_exact, dense)
+    assert gpu.device_error() == 0
 
 
 def test_config2_q6k_m256(gpu):

@@ -1,11 +1,12 @@
-"""GPU: the allocation-free split-K product (jk_matmul_splitk_noalloc) against the existing
-split-K entry point (jk_matmul_plan with a growable jk_split_scratch), through the C ABI.
+"""GPU: the allocation-free split-K product (jk_matmul_splitk_noalloc), through the C ABI, against
+the f64 oracle and against the existing split-K entry point (jk_matmul_plan with a growable
+jk_split_scratch).
 
 The allocation-free variant exists for callers that cannot allocate device memory while a product
-runs (a framework owning every device allocation, code inside a stream capture, latency paths
-that cannot afford cudaMalloc's device synchronisation): its scratch is a fixed buffer inside
-libjk.so. It must give the same products, within the library tolerance, call after call -- the
-buffer keeps the previous call's contents, so two calls in a row check that nothing stale leaks.
+runs (a framework owning every device allocation, latency paths that cannot afford cudaMalloc's
+device synchronisation): its scratch is a fixed buffer inside libjk.so. It must give the same
+products, within the library tolerance, call after call -- the buffer keeps the previous call's
+contents, so two calls in a row check that nothing stale leaks.
 
 This file is named to be collected last, so a run that stops at the first failure has already
 run every other test.
@@ -40,12 +41,13 @@ def test_noalloc_matches_scratch_product_twice(gpu, name, n, k, m, bm):
     check(load().jk_matmul_plan(w.handle, ctypes.c_void_p(x.data_ptr()), 2, x.numel(), m,
                                 ctypes.c_void_p(ref.data_ptr()), ref.numel(), scratch.handle, Plan(bm, 128, 2),
                                 ctypes.c_void_p(torch.cuda.current_stream().cuda_stream)))
-    want = ref.cpu().numpy().astype(np.float64)
+    ref_np = ref.cpu().numpy().astype(np.float64)
     for call in range(2):  # the second call runs on the buffer the first one left behind
         out = torch.full((m, n), float("nan"), device="cuda")
         check(noalloc(w, x, m, out, bm))
         got = out.cpu().numpy()
-        assert_close(f"{name} noalloc call {call}", got, x_exact, dense, want=want)
+        assert_close(f"{name} noalloc call {call} vs oracle", got, x_exact, dense)
+        assert_close(f"{name} noalloc call {call} vs jk_matmul_plan", got, x_exact, dense, want=ref_np)
     assert gpu.device_error() == 0
 
 

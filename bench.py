@@ -10,10 +10,13 @@ activation rows -- the size the metric is quoted at. One step is one pass over a
 L=36 distinct weight matrices (36 x 14.7 MB = 531 MB of weights, > 4x the 126 MB L2, so every
 matrix streams from HBM), each product writing its own f32 output. Synthetic seeded data.
 
-With N GPUs (one process per GPU, NCCL): the projection is column-sharded -- every rank owns a
+With N GPUs (one process per GPU): the projection is column-sharded -- every rank owns a
 10240-column shard of an N*10240-wide layer (per-GPU work fixed: weak scaling) -- and each
-layer's f32 output shard is all-gathered over NVLink (torch.distributed / NCCL) on a second
-stream, overlapped with the next layer's product.
+layer's f32 output shard is all-gathered over NVLink by jk_sharded_matmul_allgather: the copy
+engines push it into every peer's buffer (CUDA IPC) while the next layer's product runs, and the
+step ends with one bounded flag wait. `vocab_head` is BASELINE config 4 strong-scaled over the N
+GPUs (M=2048, K=2560, N=262144 split by column, f32 logits all-gathered), compute-only and end to
+end against max(compute, NVLink) time.
 
 Printed JSON (rank 0): `value` = aggregate TFLOP/s of the timed steps (inputs resident in HBM,
 device-timed with CUDA events, max over ranks); `e2e` = the same metric through the public API with
@@ -42,7 +45,10 @@ for p in (os.path.join(REPO, "jevons-rs_b200"), REPO):
 import numpy as np  # noqa: E402
 
 K_DIM, N_DIM, M_ROWS, LAYERS = 2560, 10240, 256, 36
-VOCAB_N = 262144  # config 4's vocabulary: the M=1 product over its head matrix
+VOCAB_N = 262144  # config 4's vocabulary: the head matrix [VOCAB_N, K_DIM]
+VOCAB_M = 2048    # config 4's rows: 8 requests x 256-token blocks
+VOCAB_CHUNKS = 8  # row chunks of the sharded head: chunk i's copies overlap chunk i+1's product
+NVLINK_GBS = 770.0  # measured peer-copy bandwidth per direction per B200 on this pool
 METRIC = "Q4_K GEMM TFLOP/s (M=256)"
 WORKLOAD = "q4k_ffn_up_m256"
 Q4_K = 12
@@ -403,7 +409,7 @@ def run_ours(args):
 
     from jevons_kernels import synth
     from jevons_kernels.gemm import Buf, Gpu, Plan, QMatrix, SplitScratch, matmul, matvec
-    from jevons_kernels.shard import column_shard, gather_shards
+    from jevons_kernels.shard import PeerGather, column_shard, shard_rows
 
     gpu = Gpu(local)
     dev = torch.device("cuda", local)
@@ -423,23 +429,18 @@ def run_ours(args):
     xb = Buf(x)
     obufs = [Buf(o) for o in outs]
 
-    comm_stream = torch.cuda.Stream(device=dev) if world > 1 else None
-    gathered = [torch.empty(world, M_ROWS, N_DIM, device=dev) for _ in range(L)] if world > 1 else None
+    # N > 1: every layer writes its own gathered [N, M, N_DIM] buffer; the copies of layer i run
+    # beside the product of layer i+1, and the step ends with one wait for all L layers.
+    pg = PeerGather(gpu, M_ROWS, N_DIM, buffers=L) if world > 1 else None
 
     def step(xbuf=xb):
-        cur = torch.cuda.current_stream()
-        for i in range(L):
-            matmul(gpu, xbuf, M_ROWS, ws[i], obufs[i], None, scratch)
-            if world > 1:
-                ev = torch.cuda.Event()
-                ev.record(cur)
-                comm_stream.wait_event(ev)
-                with torch.cuda.stream(comm_stream):
-                    gather_shards(outs[i], out=gathered[i])
         if world > 1:
-            ev = torch.cuda.Event()
-            ev.record(comm_stream)
-            cur.wait_event(ev)
+            for i in range(L):
+                pg.run(ws[i], x, i=i, wait=False, chunks=1, scratch=scratch)
+            pg.wait(L)
+        else:
+            for i in range(L):
+                matmul(gpu, xbuf, M_ROWS, ws[i], obufs[i], None, scratch)
 
     def barrier():
         torch.cuda.synchronize()
@@ -543,11 +544,11 @@ def run_ours(args):
         i = e2e_state["i"]
         e2e_state["i"] = (i + 1) % L
         xd.copy_(xh, non_blocking=True)
-        matmul(gpu, xdb, M_ROWS, ws[i], obufs[i], None, scratch)
         if world > 1:
-            gather_shards(outs[i], out=gathered[i])
-            oh.copy_(gathered[i], non_blocking=True)
+            pg.run(ws[i], xd, i=i, wait=True, chunks=2, scratch=scratch)
+            oh.copy_(pg.output(i), non_blocking=True)
         else:
+            matmul(gpu, xdb, M_ROWS, ws[i], obufs[i], None, scratch)
             oh[0].copy_(outs[i], non_blocking=True)
 
     e_steps = max(args.steps, 2 * L)
@@ -565,24 +566,62 @@ def run_ours(args):
     f16_ms = timed(step16, args.steps, args.warmup)
     f16_tflops = flops_step * world * args.steps / (f16_ms * 1e-3) / 1e12
 
-    # ---- GEMV at config 4's K, N (M=1 over a 377 MB Q4_K matrix, larger than L2) --------------
-    gv4 = None
-    if not args.no_vocab_gemv:
-        raw4 = synth.q4k_blocks(np.random.default_rng(40 + rank), VOCAB_N, K_DIM)
-        w4 = QMatrix.upload(gpu, Q4_K, VOCAB_N, K_DIM, 1, raw4)
+    # ---- config 4's matrix: the vocabulary head, Q4_K [262144, 2560] --------------------------
+    # Every rank draws the same full matrix and keeps its column shard.
+    gv4 = vocab = None
+    if not args.no_vocab:
+        raw4 = synth.q4k_blocks(np.random.default_rng(40), VOCAB_N, K_DIM)
+        v_lo, v_hi = column_shard(VOCAB_N, world, rank)
+        n_r = v_hi - v_lo
+        w4 = QMatrix.upload(gpu, Q4_K, n_r, K_DIM, 1,
+                            np.frombuffer(shard_rows(raw4, Q4_K, VOCAB_N, K_DIM, v_lo, v_hi), np.uint8))
         del raw4
-        o4 = torch.empty(1, VOCAB_N, device=dev)
-        o4b = Buf(o4)
+        if world == 1:  # M=1 product over the whole 377 MB matrix (larger than L2)
+            o4 = torch.empty(1, VOCAB_N, device=dev)
+            o4b = Buf(o4)
 
-        def gemv4():
-            matvec(gpu, x1b, 1, w4, o4b)
-        g4_steps = 20
-        g4_ms = timed(gemv4, g4_steps, 3)
-        wb4 = VOCAB_N * K_DIM // 256 * 144
-        gv4 = {"metric": "Q4_K GEMV weight-GB/s (M=1, K=2560, N=262144: config 4's matrix, 377 MB > L2)",
-               "value": wb4 * g4_steps / (g4_ms * 1e-3) / 1e9, "unit": "GB/s",
-               "frac_of_hbm": wb4 * g4_steps / (g4_ms * 1e-3) / 1e9 / pk.get("hbm_gbs", 1.0),
-               "us_per_product": g4_ms / g4_steps * 1e3}
+            def gemv4():
+                matvec(gpu, x1b, 1, w4, o4b)
+            g4_steps = 20
+            g4_ms = timed(gemv4, g4_steps, 3)
+            wb4 = VOCAB_N * K_DIM // 256 * 144
+            gv4 = {"metric": "Q4_K GEMV weight-GB/s (M=1, K=2560, N=262144: config 4's matrix, 377 MB > L2)",
+                   "value": wb4 * g4_steps / (g4_ms * 1e-3) / 1e9, "unit": "GB/s",
+                   "frac_of_hbm": wb4 * g4_steps / (g4_ms * 1e-3) / 1e9 / pk.get("hbm_gbs", 1.0),
+                   "us_per_product": g4_ms / g4_steps * 1e3}
+        # M=2048 head, strong-scaled: compute-only, then product + all-gather of the f32 logits
+        mv = VOCAB_M
+        xv = torch.from_numpy(synth.activations(np.random.default_rng(44), mv, K_DIM)).to(dev).bfloat16()
+        ov = torch.empty(mv, n_r, device=dev)
+        xvb, ovb = Buf(xv), Buf(ov)
+        v_steps = 5
+
+        def head_compute():
+            matmul(gpu, xvb, mv, w4, ovb, None, scratch)
+        c_ms = timed(head_compute, v_steps, 3) / v_steps
+        flops_v = 2.0 * mv * VOCAB_N * K_DIM
+        vplan = Plan.heuristic(w4, mv, False)
+        e_v_ms = c_ms
+        if world > 1:
+            del ov, ovb
+            pgv = PeerGather(gpu, mv, n_r, buffers=1)
+
+            def head_e2e():
+                pgv.run(w4, xv, i=0, wait=True, chunks=VOCAB_CHUNKS, scratch=scratch)
+            e_v_ms = timed(head_e2e, v_steps, 2) / v_steps
+        gather_bytes = (world - 1) * mv * n_r * 4  # each GPU sends its shard to every peer (and receives as much)
+        t_comp = flops_v / world / (pk.get("bf16_tflops", 1.0) * 1e12) * 1e3
+        t_link = gather_bytes / (NVLINK_GBS * 1e9) * 1e3
+        vocab = {"what": "BASELINE config 4: Q4_K vocab head M=2048 x K=2560 -> N=262144, column-split over "
+                         f"{world} GPU(s), f32 logits all-gathered by copy engines (jk_sharded_matmul_allgather, "
+                         f"{VOCAB_CHUNKS} row chunks); CUDA graph replay, CUDA events, max over ranks",
+                 "plan": repr(vplan), "n_per_gpu": n_r,
+                 "compute_ms": c_ms, "compute_tflops_total": flops_v / (c_ms * 1e-3) / 1e12,
+                 "e2e_ms": e_v_ms, "e2e_tflops_total": flops_v / (e_v_ms * 1e-3) / 1e12,
+                 "gather_bytes_sent_per_gpu": gather_bytes,
+                 "roofline": {"compute_ms": t_comp, "nvlink_ms": t_link, "bound": "nvlink" if t_link > t_comp else "tensor",
+                              "frac": max(t_comp, t_link) / e_v_ms, "nvlink_gbs": NVLINK_GBS,
+                              "peak_tflops": pk.get("bf16_tflops")}}
         del w4
 
     # ---- expert-grouped products (the reference's routed workloads), one GPU only -------------
@@ -608,7 +647,7 @@ def run_ours(args):
             "config": {"workload": WORKLOAD, "weights": "Q4_K", "m": M_ROWS, "k": K_DIM, "n_per_gpu": N_DIM,
                        "n_total": N_DIM * world, "layers_per_step": L, "plan": repr(plan),
                        "l2": "inputs larger than L2: 36 distinct weight matrices (531 MB) per step",
-                       "parallelism": f"column-shard x{world}" + (" + NCCL all-gather of f32 outputs" if world > 1 else ""),
+                       "parallelism": f"column-shard x{world}" + (" + copy-engine all-gather of f32 outputs over NVLink" if world > 1 else ""),
                        "activations": "bf16 N(0,1)"},
             "roofline": {"bound": "tensor", "achieved": achieved, "peak": peak, "unit": "TFLOP/s",
                          "frac": achieved / peak, "traffic": traffic,
@@ -629,7 +668,10 @@ def run_ours(args):
             "f16": {"metric": "Q4_K GEMM TFLOP/s (M=256), FP16 activations (the reference's operand type)",
                     "value": f16_tflops, "unit": "TFLOP/s", "ms_per_step": f16_ms / args.steps},
             "gemv_vocab": gv4,
-            "gpu_launches": args.steps * L * launches_per_product,
+            "vocab_head": vocab,
+            # per step: one tensor-core kernel per layer; with N GPUs also one signal kernel per peer
+            # and layer (on the copy streams) and one wait kernel
+            "gpu_launches": args.steps * (L * launches_per_product + ((world - 1) * L + 1 if world > 1 else 0)),
             "timing": "CUDA graph replay of each step, CUDA events, max over ranks",
             "clocks": sampler.report(),
             "cpu_baseline": cpu,
@@ -652,7 +694,7 @@ def main():
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--no-grouped", action="store_true", help="skip the expert-grouped workloads")
     ap.add_argument("--no-head", action="store_true", help="skip the Q6_K embedding-table workloads")
-    ap.add_argument("--no-vocab-gemv", action="store_true", help="skip the M=1 product over config 4's matrix")
+    ap.add_argument("--no-vocab", action="store_true", help="skip config 4's head (M=1 and M=2048, sharded)")
     ap.add_argument("--head-only", action="store_true", help="run only the Q6_K embedding-table workloads")
     ap.add_argument("--head-vocab", type=int, default=HEAD_VOCAB, help="table rows of the head workloads")
     args = ap.parse_args()

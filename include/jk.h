@@ -215,6 +215,29 @@ jk_status jk_f16_linear(const void *x_f16, size_t m, size_t k, const void *w_f16
 jk_status jk_f16_linear_scaled(const float *x_f32, size_t m, size_t k, const void *w_f16, size_t n,
                                float *out, jk_split_scratch *scratch, void *stream);
 
+/* ---- Q8_0 int8 path ----------------------------------------------------------------------------
+ * The int8 plan of the reference (docs/cubecl-int8-plan.md:48-60; it has no implementation there):
+ * activations are quantized per 32 values so that every Q8_0 weight block meets an activation
+ * block as an exact int32 dot product (one tcgen05 kind::i8 MMA with K = 32 per block), and the
+ * two block scales are applied in f32 afterwards. */
+
+/* Per-32 activation quantization of x [m, k] (f32, f16 or bf16; k % 32 == 0): for each row r and
+ * block b, amax = max |x[r, 32b..32b+31]|, d = amax / 127 and q = rint(x * (127 / amax)) clamped
+ * to [-127, 127] (IEEE f32, round to nearest even; an all-zero block gives d = 0, q = 0).
+ * xq: int8 [m, k] (xq_len >= m * k); xd: f32 scales, block-major [k / 32][m_pad] with m_pad = m
+ * rounded up to a multiple of 4 (xd_len >= k / 32 * m_pad; the padding rows are set to 0).
+ * Deterministic; asynchronous on `stream`. */
+jk_status jk_quantize_act_q8(const void *x, int x_dtype, size_t m, size_t k, int8_t *xq, size_t xq_len,
+                             float *xd, size_t xd_len, void *stream);
+
+/* The Q8_0 product on int8 tensor cores: out[r, c] = sum over blocks b, in increasing order, of
+ *   f32(dot_b) * (f32(d_w[c, b]) * xd[b][r])   accumulated with one fused multiply-add per block,
+ * where dot_b = sum_j q_w[c, 32b + j] * xq[r, 32b + j] is exact in int32. w must be Q8_0 (expert 0's
+ * rows for a multi-expert matrix); xq / xd as written by jk_quantize_act_q8 for the same m and
+ * k (16-byte aligned); out f32 [m, n]. JK_ERR_UNSUPPORTED for other weight types. */
+jk_status jk_matmul_q8_int8(const jk_qmatrix *w, const int8_t *xq, size_t xq_len, const float *xd,
+                            size_t xd_len, size_t m, float *out, size_t out_len, void *stream);
+
 /* ---- expert-grouped products ----------------------------------------------------------------- */
 
 /* Groups (gemm.rs:955-966): a device-side grouping of routed rows by expert, as written by
@@ -262,6 +285,51 @@ jk_status jk_matmul_grouped(const jk_qmatrix *w, const void *x, int x_dtype, siz
  * with tiles of mr <= JK_GEMV_ROWS rows. Reads activation rows in place (no scratch). */
 jk_status jk_matvec_grouped(const jk_qmatrix *w, const void *x, int x_dtype, size_t x_len, const jk_groups *g,
                             float *out, size_t out_len, int mr, void *stream);
+
+/* ---- column-sharded product across GPUs ---------------------------------------------------------
+ * The multi-GPU layout of the large-N projections (the vocabulary head, the FFN up projection):
+ * no counterpart in the reference, which runs on one device. Rank r of `world` (one process or
+ * thread per GPU, world <= 8) holds its shard w_shard = weight rows [r n_r, (r + 1) n_r) of the
+ * full [world n_r, k] matrix, and every rank ends with the whole f32 output in a rank-major buffer
+ * [world][m][n_r]: rank p's output columns are rows [p m, (p + 1) m) of it. */
+
+/* Device memory another process can map: cudaMalloc of `bytes` (zeroed) on `device` and its
+ * 64-byte CUDA IPC handle. Free with jk_ipc_free. */
+jk_status jk_ipc_alloc(int device, size_t bytes, void **dev_ptr, uint8_t handle[64]);
+jk_status jk_ipc_free(int device, void *dev_ptr);
+/* Maps another process's jk_ipc_alloc buffer on `device` (peer access enabled); unmap with
+ * jk_ipc_close. */
+jk_status jk_ipc_open(int device, const uint8_t handle[64], void **dev_ptr);
+jk_status jk_ipc_close(int device, void *dev_ptr);
+
+/* out_peers[p] (p < world): rank p's gathered output buffer [world][m][n_r] f32 as mapped in this
+ * process (this rank's own at p == rank); flags_peers[p]: rank p's `world` u32 flag words.
+ * The product of x [m, k] with the shard (jk_matmul's heuristic plan) is computed in `chunks`
+ * row chunks (1..16, multiples of 32 rows) into this rank's block of its own buffer; each finished
+ * chunk is pushed into every peer's buffer by the copy engines (one copy stream per peer, inside
+ * the library) while the next chunk's product runs, so the exchange takes no SMs from the product.
+ * After its copies the rank adds one to flags_peers[p][rank] in every peer (a system-scope
+ * reduction ordered after the copies); a rank's own slot flags[rank] counts the calls it has
+ * waited for. With wait != 0, `stream` then joins this rank's copies and a one-warp kernel waits
+ * until every peer's counter has reached this call (every peer's shard has landed): the gathered
+ * output is complete on `stream` after the call. With wait == 0 the call returns with the copies
+ * still running beside `stream` (the next product can overlap them): this rank's block of
+ * out_peers[rank] must then stay untouched, and the caller ends the exchange with
+ * jk_allgather_wait(..., calls, ...) for the `calls` products made with these flags since the
+ * last wait (for example once after several layers, each with its own output buffers). All ranks
+ * make the same calls in the same order. The counters live on the device, so a captured CUDA graph
+ * that replays these calls stays in step. Waits are bounded (2 s): a peer that never signals sets
+ * ERR_WAIT_TIMEOUT, read with jk_device_error. A result stays valid until the next call on any
+ * rank that writes the same buffers. Inside a CUDA graph capture, jk_allgather_wait joins copies
+ * issued in the same capture only. */
+jk_status jk_sharded_matmul_allgather(const jk_qmatrix *w_shard, const void *x, int x_dtype, size_t x_len,
+                                      size_t m, int rank, int world, float *const *out_peers,
+                                      uint32_t *const *flags_peers, int chunks, int wait,
+                                      jk_split_scratch *scratch, void *stream);
+/* Joins this rank's outstanding copies on `stream`, then waits until every peer's counter in
+ * flags (this rank's flag words) has reached flags[rank] + calls, and advances flags[rank]
+ * (bounded, as above). */
+jk_status jk_allgather_wait(int device, uint32_t *flags, int world, int rank, uint32_t calls, void *stream);
 
 /* ---- allocation-free product ----------------------------------------------------------------- */
 

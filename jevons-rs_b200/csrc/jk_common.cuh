@@ -174,6 +174,27 @@ __device__ __forceinline__ bool mbar_wait(uint32_t bar, uint32_t parity, uint32_
     }
 }
 
+// The same wait with cluster-scope acquire: for barriers that the other CTA of a pair arrives on
+// (its writes before a release.cluster arrive are visible after this wait).
+__device__ __forceinline__ bool mbar_try_wait_cluster(uint32_t bar, uint32_t parity) {
+    uint32_t ok;
+    asm volatile(
+        "{ .reg .pred p; mbarrier.try_wait.parity.acquire.cluster.shared::cta.b64 p, [%1], %2; selp.u32 %0, 1, 0, p; }"
+        : "=r"(ok) : "r"(bar), "r"(parity) : "memory");
+    return ok != 0;
+}
+__device__ __forceinline__ bool mbar_wait_cluster(uint32_t bar, uint32_t parity, uint32_t* err) {
+    if (mbar_try_wait_cluster(bar, parity)) return true;
+    const uint64_t t0 = globaltimer();
+    for (uint32_t i = 1;; ++i) {
+        if (mbar_try_wait_cluster(bar, parity)) return true;
+        if ((i & 63u) == 0 && globaltimer() - t0 > WAIT_LIMIT_NS) {
+            atomicOr(err, ERR_WAIT_TIMEOUT);
+            return false;
+        }
+    }
+}
+
 // For waits expected to last long (an epilogue waiting for a whole main loop): after a short spin,
 // sleep between polls so the waiting warps leave their issue slots to the working warps.
 __device__ __forceinline__ bool mbar_wait_sleepy(uint32_t bar, uint32_t parity, uint32_t* err) {

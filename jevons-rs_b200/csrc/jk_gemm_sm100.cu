@@ -135,13 +135,20 @@ struct Smem {
     // barrier pair serves the activations and the weights of the stage, so the MMA issuer and the
     // dequantizers wait once per four k-blocks (an mbarrier wait costs about as much issue time as
     // four M=128, N=32 MMAs).
-    static constexpr bool TMEM_A = FMT != FMT_F16 && !PAIR && BT <= 128;
+    //
+    // CTA pairs with 256-row activation tiles use tensor-memory stages too (the M = 256 MMA reads
+    // each CTA's 128 weight rows from that CTA's tensor memory): one 256-column accumulator per
+    // CTA (NACC = 1) leaves room for two stages. A pair then decodes every weight tile once per
+    // 256 activation rows and each SM's MMA (128 x 256 x 64 per k-block) outlasts its decoding.
+    static constexpr bool TMEM_A = FMT != FMT_F16 && (PAIR ? BT == 256 : BT <= 128);
     static constexpr int KPS = TMEM_A ? 4 : 1;                  // k-blocks per stage
     static constexpr int B_ATOM = (PAIR ? BT / 2 : BT) * 128;  // one k-block of activations (a pair CTA: half the rows)
     static constexpr int B_STAGE = KPS * B_ATOM;
     static constexpr int raw_bytes = RawTile<FMT>::bytes;
-    static constexpr uint32_t TMEM_A0 = 2 * BT;  // first tensor-memory column of the A stages
-    static constexpr Rings rings = TMEM_A ? pick_rings_tmem(B_STAGE, raw_bytes, (512 - 2 * BT) / (32 * KPS))
+    // accumulator buffers (the epilogue of one tile overlaps the MMAs of the next when there are 2)
+    static constexpr int NACC = TMEM_A && 2 * BT + 2 * 32 * KPS > 512 ? 1 : 2;
+    static constexpr uint32_t TMEM_A0 = NACC * BT;  // first tensor-memory column of the A stages
+    static constexpr Rings rings = TMEM_A ? pick_rings_tmem(B_STAGE, raw_bytes, (512 - NACC * BT) / (32 * KPS))
                                           : pick_rings(B_STAGE, raw_bytes);
     static constexpr int SX = rings.sx, SA = rings.sa, R = rings.r;
     // Groups of 4 dequantizer warps. A TMEM_A group waits on a stage's empty barrier by phase
@@ -152,7 +159,7 @@ struct Smem {
     static constexpr int THREADS = TMEM_A ? 32 * (8 + 4 * DQ_GROUPS) : 512;
     static_assert(!TMEM_A || (DQ_GROUPS >= 2 && DQ_GROUPS <= SA), "dequantizer groups vs stages");
     static_assert(FMT != FMT_F16 || SX == SA, "FP16 weights share the activation ring");
-    static constexpr uint32_t TMEM_COLS = TMEM_A ? 512 : 2 * BT;
+    static constexpr uint32_t TMEM_COLS = TMEM_A ? 512 : NACC * BT;
     static_assert(!TMEM_A || (SX == SA && TMEM_A0 + 32 * KPS * SA <= TMEM_COLS), "tensor memory budget");
     static constexpr int off_b = 0;
     static constexpr int off_a = off_b + SX * B_STAGE;
@@ -302,6 +309,14 @@ __device__ __forceinline__ void mma_f16_pair(uint32_t d_tmem, uint64_t a_desc, u
     asm volatile(
         "{ .reg .pred p; setp.ne.b32 p, %4, 0; tcgen05.mma.cta_group::2.kind::f16 [%0], %1, %2, %3, p; }"
         :: "r"(d_tmem), "l"(a_desc), "l"(b_desc), "r"(idesc), "r"(accumulate) : "memory");
+}
+// the same with A read from tensor memory: each CTA's tensor memory holds its 128 rows of A at the
+// same address (two 16-bit values per 32-bit column in k order)
+__device__ __forceinline__ void mma_f16_ta_pair(uint32_t d_tmem, uint32_t a_tmem, uint64_t b_desc, uint32_t idesc,
+                                                uint32_t accumulate) {
+    asm volatile(
+        "{ .reg .pred p; setp.ne.b32 p, %4, 0; tcgen05.mma.cta_group::2.kind::f16 [%0], [%1], %2, %3, p; }"
+        :: "r"(d_tmem), "r"(a_tmem), "l"(b_desc), "r"(idesc), "r"(accumulate) : "memory");
 }
 // arrive on the mbarrier at offset `bar` in both CTAs of the pair once the issued MMAs complete
 __device__ __forceinline__ void mma_commit_pair(uint32_t bar) {
@@ -671,11 +686,12 @@ __device__ __forceinline__ void dequant_role(const Sched& sched, SegState& ss, u
 // turns: group g decodes the whole stage st with st % G == g (one super-block header decode, one
 // raw wait and one empty wait per 4 k-blocks per group) into TMEM lanes of its rows, one
 // tcgen05.st of 32 columns per k-block, then arrives once on the stage's full barrier.
-template <int FMT, bool BF16, int BT>
+template <int FMT, bool BF16, int BT, bool PAIR>
 __device__ __forceinline__ void dequant_role_tmem(const Sched& sched, SegState& ss, uint8_t* smem, int row_in_tile,
-                                                  int grp, const WView& w, uint32_t* err, bool& ok, uint32_t bar0,
-                                                  int lane, uint32_t tmem) {
-    using L = Smem<FMT, BT, false>;
+                                                  int grp, int rank, const WView& w, uint32_t* err, bool& ok,
+                                                  uint32_t bar0, int lane, uint32_t tmem) {
+    using L = Smem<FMT, BT, PAIR>;
+    constexpr int TW = PAIR ? 2 * BW : BW;  // weight rows per tile
     constexpr int S = L::SX, R = L::R, KPS = L::KPS;
     static_assert(KPS == 4, "a stage is one raw super-block");
     constexpr int G = L::DQ_GROUPS;
@@ -689,7 +705,7 @@ __device__ __forceinline__ void dequant_role_tmem(const Sched& sched, SegState& 
     int st = 0;  // stage = raw super-block counter
     Seg sg;
     while (ok && seg_next(sched, ss, sg)) {
-        const int64_t row = tile_at<BW, BT>(sched, sg.tile, 0, 0).wrow0 + row_in_tile;
+        const int64_t row = tile_at<TW, BT>(sched, sg.tile, rank, 0).wrow0 + row_in_tile;
         const bool row_ok = row < w.rows;
         const int64_t rr = row_ok ? row : 0;
         const int sb_lo = sg.kb_lo >> 2, sb_hi = (sg.kb_hi - 1) >> 2;
@@ -730,7 +746,8 @@ __device__ __forceinline__ void dequant_role_tmem(const Sched& sched, SegState& 
             __syncwarp();
             JK_TRACE_POINT(9, st);
             if (lane == 0) {
-                mbar_arrive(full(s));
+                if constexpr (PAIR) mbar_arrive_cluster(mapa_shared(full(s), 0));  // the leader issues the MMA
+                else mbar_arrive(full(s));
                 mbar_arrive(raw_empty(slot));
             }
         }
@@ -781,8 +798,8 @@ gemm_tc_kernel(const __grid_constant__ CUtensorMap tm_x, const __grid_constant__
     if (threadIdx.x == 0) {
         for (int s = 0; s < SX; ++s) {
             // TMEM_A: the stage's producer arrival (with its bytes) and the warps of the
-            // dequantizer group that decodes the stage
-            mbar_init(full_b(s), L::TMEM_A ? 1 + 4 : 1);
+            // dequantizer group that decodes the stage (in both CTAs of a pair, on the leader's barrier)
+            mbar_init(full_b(s), L::TMEM_A ? 1 + 4 * (PAIR ? 2 : 1) : 1);
             mbar_init(empty_b(s), 1);
         }
         for (int s = 0; s < SA; ++s) {
@@ -846,7 +863,8 @@ gemm_tc_kernel(const __grid_constant__ CUtensorMap tm_x, const __grid_constant__
         if constexpr (L::TMEM_A) {
             constexpr int KPS = L::KPS;
             while (ok && seg_next(sched, ss, sg)) {
-                const int32_t m0 = (int32_t)tile_at<TW, BT>(sched, sg.tile, rank, m).m0;
+                const int32_t m0 =
+                    (int32_t)(tile_at<TW, BT>(sched, sg.tile, rank, m).m0 + (PAIR ? rank * (BT / 2) : 0));
                 for (int p = sg.kb_lo / KPS; p <= (sg.kb_hi - 1) / KPS && ok; ++p) {
                     const int s = it % SX;
                     if (it >= SX) ok = __all_sync(0xFFFFFFFFu, mbar_wait(empty_b(s), ((it / SX) - 1) & 1, err));
@@ -855,10 +873,19 @@ gemm_tc_kernel(const __grid_constant__ CUtensorMap tm_x, const __grid_constant__
                     const int lo = p * KPS > sg.kb_lo ? p * KPS : sg.kb_lo;
                     const int hi = p * KPS + KPS < sg.kb_hi ? p * KPS + KPS : sg.kb_hi;
                     if (elect_one()) {
-                        mbar_expect_tx(full_b(s), (uint32_t)((hi - lo) * L::B_ATOM));
-                        for (int kb = lo; kb < hi; ++kb)
-                            tma_load_2d(sbase + L::off_b + s * L::B_STAGE + (kb % KPS) * L::B_ATOM, &tm_x, kb * KB, m0,
-                                        full_b(s));
+                        if constexpr (PAIR) {
+                            // both CTAs' halves count on the leader's barrier; only the leader expects them
+                            if (rank == 0) mbar_expect_tx(full_b(s), (uint32_t)(2 * (hi - lo) * L::B_ATOM));
+                            const uint32_t lbar = mapa_shared(full_b(s), 0);
+                            for (int kb = lo; kb < hi; ++kb)
+                                tma_load_2d_pair(sbase + L::off_b + s * L::B_STAGE + (kb % KPS) * L::B_ATOM, &tm_x,
+                                                 kb * KB, m0, lbar);
+                        } else {
+                            mbar_expect_tx(full_b(s), (uint32_t)((hi - lo) * L::B_ATOM));
+                            for (int kb = lo; kb < hi; ++kb)
+                                tma_load_2d(sbase + L::off_b + s * L::B_STAGE + (kb % KPS) * L::B_ATOM, &tm_x, kb * KB,
+                                            m0, full_b(s));
+                        }
                     }
                     __syncwarp();
                     ++it;
@@ -941,9 +968,10 @@ gemm_tc_kernel(const __grid_constant__ CUtensorMap tm_x, const __grid_constant__
             if constexpr (PAIR) mma_commit_pair(bar);
             else mma_commit(bar);
         };
+        constexpr int NACC = L::NACC;
         while (ok && seg_next(sched, ss, sg)) {
-            const int b = seg_i & 1;
-            if (seg_i >= 2) ok = __all_sync(0xFFFFFFFFu, mbar_wait(acc_empty(b), ((seg_i >> 1) - 1) & 1, err));
+            const int b = seg_i % NACC;
+            if (seg_i >= NACC) ok = __all_sync(0xFFFFFFFFu, mbar_wait(acc_empty(b), ((seg_i / NACC) - 1) & 1, err));
             if (!ok) break;
             tc_fence_after();
             const uint32_t acc = tmem + (uint32_t)(b * BT);
@@ -954,7 +982,9 @@ gemm_tc_kernel(const __grid_constant__ CUtensorMap tm_x, const __grid_constant__
                 for (int p = sg.kb_lo / KPS; p <= (sg.kb_hi - 1) / KPS; ++p) {
                     const int s = it % SX;
                     JK_TRACE_POINT(2, it);
-                    ok = __all_sync(0xFFFFFFFFu, mbar_wait(full_b(s), (uint32_t)((it / SX) & 1), err));
+                    // (a pair's stage is complete when the other CTA's dequantizers have arrived too)
+                    ok = __all_sync(0xFFFFFFFFu, PAIR ? mbar_wait_cluster(full_b(s), (uint32_t)((it / SX) & 1), err)
+                                                      : mbar_wait(full_b(s), (uint32_t)((it / SX) & 1), err));
                     if (!ok) break;
                     JK_TRACE_POINT(4, it);
                     tc_fence_after();
@@ -969,9 +999,13 @@ gemm_tc_kernel(const __grid_constant__ CUtensorMap tm_x, const __grid_constant__
                             const int kb = p * KPS + j;
                             if (kb < sg.kb_lo || kb >= sg.kb_hi) continue;
 #pragma unroll
-                            for (int k = 0; k < KB / 16; ++k)
-                                mma_f16_ta(acc, at + (uint32_t)(32 * j + 8 * k), bd + (uint64_t)(j * (L::B_ATOM >> 4) + 2 * k),
-                                           IDESC, (kb > sg.kb_lo || k > 0) ? 1u : 0u);
+                            for (int k = 0; k < KB / 16; ++k) {
+                                const uint32_t a_k = at + (uint32_t)(32 * j + 8 * k);
+                                const uint64_t b_k = bd + (uint64_t)(j * (L::B_ATOM >> 4) + 2 * k);
+                                const uint32_t accum = (kb > sg.kb_lo || k > 0) ? 1u : 0u;
+                                if constexpr (PAIR) mma_f16_ta_pair(acc, a_k, b_k, IDESC, accum);
+                                else mma_f16_ta(acc, a_k, b_k, IDESC, accum);
+                            }
                         }
                         JK_TRACE_POINT(0, it);
                         commit(empty_b(s));
@@ -1039,10 +1073,10 @@ gemm_tc_kernel(const __grid_constant__ CUtensorMap tm_x, const __grid_constant__
         if (!ok && issued) {
             // Error path: drain the MMAs issued so far before TMEM is released. The commit arrives on
             // acc_full(b) of the unfinished segment; wait for it.
-            const int b = seg_i & 1;
+            const int b = seg_i % NACC;
             if (leader) commit(acc_full(b));
             __syncwarp();
-            mbar_wait(acc_full(b), (seg_i >> 1) & 1, err);
+            mbar_wait(acc_full(b), (seg_i / NACC) & 1, err);
         }
     } else if (warp >= EPI_WARP0 && warp < EPI_WARP0 + EPI_WARPS) {
         // ------------------------------ epilogue ------------------------------
@@ -1055,8 +1089,8 @@ gemm_tc_kernel(const __grid_constant__ CUtensorMap tm_x, const __grid_constant__
         int seg_i = 0;
         int fix_q = 0;  // fix-up chunks consumed so far (ring parity)
         while (ok && seg_next(sched, ss, sg)) {
-            const int b = seg_i & 1;
-            ok = __all_sync(0xFFFFFFFFu, mbar_wait_sleepy(acc_full(b), (seg_i >> 1) & 1, err));
+            const int b = seg_i % L::NACC;
+            ok = __all_sync(0xFFFFFFFFu, mbar_wait_sleepy(acc_full(b), (seg_i / L::NACC) & 1, err));
             tc_fence_after();
             if (!ok) break;
             JK_TRACE_POINT(7, seg_i);
@@ -1250,7 +1284,8 @@ gemm_tc_kernel(const __grid_constant__ CUtensorMap tm_x, const __grid_constant__
             const int t = 32 * dq_slot<L::TMEM_A>(warp) + lane;  // 0..255
             const int row_in_tile = t & (BW - 1);
             if constexpr (L::TMEM_A)
-                dequant_role_tmem<FMT, BF16, BT>(sched, ss, smem, row_in_tile, t / BW, w, err, ok, bar0, lane, tmem);
+                dequant_role_tmem<FMT, BF16, BT, PAIR>(sched, ss, smem, row_in_tile, t / BW, rank, w, err, ok, bar0, lane,
+                                                       tmem);
             else
                 dequant_role<FMT, BF16, BT, PAIR>(sched, ss, smem, row_in_tile, t / BW, rank, w, err, ok, bar0, lane);
         }
@@ -1335,7 +1370,7 @@ jk_status launch_tc(const LaunchArgs& a) {
         cfg.blockDim = dim3(L::THREADS);
         cfg.dynamicSmemBytes = L::total;
         cfg.stream = a.stream;
-        cudaLaunchAttribute attr[1];
+        cudaLaunchAttribute attr[2];
         attr[0].id = cudaLaunchAttributeClusterDimension;
         attr[0].val.clusterDim.x = 2;
         attr[0].val.clusterDim.y = 1;
@@ -1361,6 +1396,11 @@ jk_status launch_tc(const LaunchArgs& a) {
         if (g < 1) g = 1;
         s.G = (int)g;
         cfg.gridDim = dim3(2 * (unsigned)s.G);
+        // programmatic dependent launch, as for single CTAs: the next product's pairs start on the
+        // SMs this grid frees and fill their weight stages while its last tiles finish
+        attr[1].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+        attr[1].val.programmaticStreamSerializationAllowed = 1;
+        cfg.numAttrs = 2;
         cudaError_t e = cudaLaunchKernelEx(&cfg, kern, *a.tm_x, a.wq->tm_w, w, a.out, a.m, a.ldo, s, a.ws_part,
                                            a.ws_flag, device_error_word(a.wq->device));
         if (e != cudaSuccess) return cuda_fail(e, "gemm pair launch");

@@ -72,6 +72,14 @@ SIGNATURES = {
     "jk_f16_linear": (I, [P, S, S, P, S, P, P]),
     "jk_f16_linear_scaled": (I, [P, S, S, P, S, P, P, P]),
     "jk_dequantize": (I, [I, P, S, P, S]),
+    "jk_quantize_act_q8": (I, [P, I, S, S, P, S, P, S, P]),
+    "jk_matmul_q8_int8": (I, [P, P, S, P, S, S, P, S, P]),
+    "jk_ipc_alloc": (I, [I, S, ctypes.POINTER(P), P]),
+    "jk_ipc_free": (I, [I, P]),
+    "jk_ipc_open": (I, [I, P, ctypes.POINTER(P)]),
+    "jk_ipc_close": (I, [I, P]),
+    "jk_sharded_matmul_allgather": (I, [P, P, I, S, S, I, I, P, P, I, I, P, P]),
+    "jk_allgather_wait": (I, [I, P, I, I, U32, P]),
     "jk_matmul_splitk_noalloc": (I, [P, P, I, S, S, P, S, I, P]),
     "jk_set_max_ctas": (I, [I, I]),
     "jk_get_max_ctas": (I, [I, ctypes.POINTER(I), ctypes.POINTER(I)]),

@@ -280,6 +280,28 @@ def matmul_splitk_noalloc(gpu: Gpu, x: Buf, m: int, w: QMatrix, out: Buf, bm: in
     check(load().jk_matmul_splitk_noalloc(w.handle, xp, xt, xl, m, op, ol, int(bm), _stream()))
 
 
+def q8_scales_len(m: int, k: int) -> int:
+    """Length of the block-major activation scales jk_quantize_act_q8 writes: k / 32 rows of m
+    rounded up to a multiple of 4."""
+    return k // 32 * ((m + 3) // 4 * 4)
+
+
+def quantize_act_q8(gpu: Gpu, x: Buf, m: int, k: int, xq: Buf, xd: Buf) -> None:
+    """Per-32 activation quantization for the Q8_0 int8 path (jk_quantize_act_q8): xq int8 [m, k],
+    xd f32 [k / 32, m_pad] block-major scales."""
+    if xq.tensor.dtype != torch.int8 or xd.tensor.dtype != torch.float32:
+        raise JkError(1, "quantize_act_q8 writes int8 quants and f32 scales")
+    check(load().jk_quantize_act_q8(x.ptr(), x.dtype_code(), int(m), int(k), xq.ptr(), xq.len(), xd.ptr(), xd.len(),
+                                    _stream()))
+
+
+def matmul_q8_int8(gpu: Gpu, w: QMatrix, xq: Buf, xd: Buf, m: int, out: Buf) -> None:
+    """The Q8_0 product on int8 tensor cores (jk_matmul_q8_int8): exact int32 block dots, scaled
+    in f32 in block order."""
+    check(load().jk_matmul_q8_int8(w.handle, xq.ptr(), xq.len(), xd.ptr(), xd.len(), int(m), out.ptr(), out.len(),
+                                   _stream()))
+
+
 class Groups:
     """Expert grouping on the device (gemm.rs:955-966): `ids` = sorted assignment indices,
     `offsets` [experts + 1], `jobs` [1 + 2 * max_jobs]; input row = id // in_div; `rows` output
@@ -379,5 +401,5 @@ def f16_linear_scaled(x: torch.Tensor, weight: torch.Tensor) -> torch.Tensor:
 
 
 __all__ = ["GEMV_ROWS", "Gpu", "Buf", "QMatrix", "Plan", "SplitScratch", "matmul", "matmul_plan", "matmul_tiled",
-           "matvec", "matmul_splitk_noalloc", "Groups", "group_max_jobs", "group_routes", "matmul_grouped",
+           "matvec", "matmul_splitk_noalloc", "q8_scales_len", "quantize_act_q8", "matmul_q8_int8", "Groups", "group_max_jobs", "group_routes", "matmul_grouped",
            "matvec_grouped", "f16_linear", "f16_linear_scaled", "tile_n", "TensorType", "block", "pack", "JkError"]

@@ -74,3 +74,111 @@ def logical_columns(gathered):
     """``[m, world, n_r]`` view of a rank-major gathered output: element [i, r, j] is output
     column r * n_r + j of row i."""
     return gathered.permute(1, 0, 2)
+
+
+class PeerGather:
+    """Buffers for jk_sharded_matmul_allgather on one rank: `buffers` rank-major gathered outputs
+    [world, m, n_r] f32 and one array of `world` u32 counter words, allocated with jk_ipc_alloc on
+    this rank's GPU and mapped into every other rank (jk_ipc_open) through one exchange of the
+    64-byte IPC handles over the process group. The copy engines of each rank write its shard into
+    the peers' buffers; nothing here launches a collective kernel. Every rank must create it and
+    call `run` / `wait` in the same order."""
+
+    def __init__(self, gpu, m: int, n_r: int, buffers: int = 2, group=None):
+        import ctypes
+        import torch.distributed as dist
+        from ._lib import check, load
+        self.gpu, self.m, self.n_r, self.buffers = gpu, int(m), int(n_r), int(buffers)
+        self.world = dist.get_world_size(group) if dist.is_initialized() else 1
+        self.rank = dist.get_rank(group) if dist.is_initialized() else 0
+        lib = load()
+        dev = gpu.device
+        self._own, handles = [], []
+        sizes = [self.world * self.m * self.n_r * 4] * self.buffers + [max(self.world * 4, 256)]
+        for nbytes in sizes:
+            ptr = ctypes.c_void_p()
+            h = (ctypes.c_uint8 * 64)()
+            check(lib.jk_ipc_alloc(dev, nbytes, ctypes.byref(ptr), h))
+            self._own.append(ptr.value)
+            handles.append(bytes(h))
+        everyone = [None] * self.world
+        if self.world > 1:
+            dist.all_gather_object(everyone, handles, group=group)
+        else:
+            everyone = [handles]
+        self._opened = []
+        # tables[i]: pointer arrays [world] of buffer i (the last entry: the flag words) per rank
+        self.tables = []
+        for i in range(len(sizes)):
+            arr = (ctypes.c_void_p * self.world)()
+            for p in range(self.world):
+                if p == self.rank:
+                    arr[p] = self._own[i]
+                    continue
+                ptr = ctypes.c_void_p()
+                h = (ctypes.c_uint8 * 64).from_buffer_copy(everyone[p][i])
+                check(lib.jk_ipc_open(dev, h, ctypes.byref(ptr)))
+                self._opened.append(ptr.value)
+                arr[p] = ptr.value
+            self.tables.append(arr)
+        self.flags = self.tables[-1]
+
+    def output(self, i: int):
+        """Gathered output buffer i as a torch tensor [world, m, n_r] (no copy)."""
+        n = self.world * self.m * self.n_r
+        return _tensor_from_ptr(self.tables[i][self.rank], n, self.gpu.device).view(self.world, self.m, self.n_r)
+
+    def run(self, w_shard, x, i: int = 0, wait: bool = True, chunks: int = 4, scratch=None, stream=None):
+        """One jk_sharded_matmul_allgather call into gathered buffer i."""
+        import ctypes
+        import torch
+        from ._lib import check, load
+        st = stream if stream is not None else torch.cuda.current_stream().cuda_stream
+        check(load().jk_sharded_matmul_allgather(
+            w_shard.handle, ctypes.c_void_p(x.data_ptr()), _DT[x.dtype], x.numel(), self.m, self.rank, self.world,
+            ctypes.cast(self.tables[i], ctypes.c_void_p), ctypes.cast(self.flags, ctypes.c_void_p), int(chunks),
+            1 if wait else 0, scratch.handle if scratch is not None else None, ctypes.c_void_p(st)))
+
+    def wait(self, calls: int, stream=None):
+        """jk_allgather_wait for the `calls` products made with wait=False since the last wait."""
+        import ctypes
+        import torch
+        from ._lib import check, load
+        st = stream if stream is not None else torch.cuda.current_stream().cuda_stream
+        check(load().jk_allgather_wait(self.gpu.device, ctypes.c_void_p(self.flags[self.rank]), self.world,
+                                       self.rank, int(calls), ctypes.c_void_p(st)))
+
+    def close(self):
+        from ._lib import load
+        lib = load()
+        for p in getattr(self, "_opened", []):
+            lib.jk_ipc_close(self.gpu.device, p)
+        for p in getattr(self, "_own", []):
+            lib.jk_ipc_free(self.gpu.device, p)
+        self._opened, self._own = [], []
+
+
+def _tensor_from_ptr(ptr: int, numel: int, device: int):
+    """A float32 CUDA tensor viewing `numel` values at device pointer `ptr` (memory owned elsewhere)."""
+    import torch
+
+    class _Cai:
+        def __init__(self):
+            self.__cuda_array_interface__ = {"shape": (numel,), "typestr": "<f4", "data": (ptr, False),
+                                             "version": 3, "strides": None}
+    with torch.cuda.device(device):
+        return torch.as_tensor(_Cai(), device=f"cuda:{device}")
+
+
+def _dtypes():
+    import torch
+    return {torch.float32: 0, torch.float16: 1, torch.bfloat16: 2}
+
+
+class _DtMap(dict):
+    def __missing__(self, key):
+        self.update(_dtypes())
+        return dict.__getitem__(self, key)
+
+
+_DT = _DtMap()

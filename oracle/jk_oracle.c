@@ -26,6 +26,12 @@
  *
  * Parity pin: the known-answer tests of crates/jevons-formats/src/quant.rs:199-237 are
  * replayed against this file by tests/test_oracle.py (fixtures in tests/golden/).
+ *
+ * The Q8_0 int8 path (jk_quantize_act_q8 / jk_matmul_q8_int8) has no counterpart that runs in
+ * the reference: its docs/cubecl-int8-plan.md:48-60 plans per-32 activation quantization with
+ * integer block dots and f32 block scales (llama.cpp's q8_1 scheme, not present here). The
+ * build's own definition of it is restated below (jko_quantize_act_q8, jko_matmul_q8_int8):
+ * parity of that path is pinned to this restatement only.
  */
 #include <math.h>
 #include <stdint.h>
@@ -297,4 +303,58 @@ int jko_max_threads(void) {
 #else
     return 1;
 #endif
+}
+
+/* ---------------------------------------------------------------------------------------------
+ * Q8_0 int8 path. Activation quantization per (row, 32-value block):
+ *   amax = max |x|, d = amax / 127, q = rint(x * (127 / amax)) clamped to [-127, 127]
+ * (IEEE f32 division and multiplication, rint = round to nearest even; amax = 0 gives q = 0,
+ * d = 0). q -> xq[row * k + j]; d -> xd[(j / 32) * m_pad + row] (block-major scales).
+ * --------------------------------------------------------------------------------------------- */
+void jko_quantize_act_q8(const float *x, size_t m, size_t k, int8_t *xq, float *xd, size_t m_pad) {
+    const size_t nblk = k / 32;
+#pragma omp parallel for schedule(static)
+    for (size_t r = 0; r < m; ++r) {
+        for (size_t b = 0; b < nblk; ++b) {
+            const float *v = x + r * k + 32 * b;
+            float amax = 0.0f;
+            for (int j = 0; j < 32; ++j) amax = fmaxf(amax, fabsf(v[j]));
+            const float d = amax / 127.0f;
+            const float id = amax > 0.0f ? 127.0f / amax : 0.0f;
+            for (int j = 0; j < 32; ++j) {
+                float q = rintf(v[j] * id);
+                q = fminf(fmaxf(q, -127.0f), 127.0f);
+                xq[r * k + 32 * b + j] = (int8_t)q;
+            }
+            xd[b * m_pad + r] = d;
+        }
+    }
+}
+
+/* The int8 product over raw GGML Q8_0 rows W [n][k/32][34 bytes]:
+ *   dot = sum_j q_w[c, 32b + j] * q_x[r, 32b + j]            (exact int32)
+ *   s   = f32(d_w[c, b]) * d_x[r, b]                          (f32 multiply)
+ *   acc = fmaf(f32(dot), s, acc)   for b = 0, 1, ... in order (one f32 rounding per block)
+ * out[r * n + c] = acc. Also returns the int32 block dots when dots != NULL:
+ * dots[(r * n + c) * nblk + b]. */
+void jko_matmul_q8_int8(const uint8_t *raw, size_t n, size_t k, const int8_t *xq, const float *xd, size_t m,
+                        size_t m_pad, float *out, int32_t *dots) {
+    const size_t nblk = k / 32;
+#pragma omp parallel for schedule(dynamic, 4)
+    for (size_t c = 0; c < n; ++c) {
+        const uint8_t *row = raw + c * nblk * 34;
+        for (size_t r = 0; r < m; ++r) {
+            float acc = 0.0f;
+            for (size_t b = 0; b < nblk; ++b) {
+                const uint8_t *blk = row + b * 34;
+                const int8_t *qx = xq + r * k + 32 * b;
+                int32_t dot = 0;
+                for (int j = 0; j < 32; ++j) dot += (int32_t)(int8_t)blk[2 + j] * (int32_t)qx[j];
+                if (dots) dots[(r * n + c) * nblk + b] = dot;
+                const float s = half_at(blk) * xd[b * m_pad + r];
+                acc = fmaf((float)dot, s, acc);
+            }
+            out[r * n + c] = acc;
+        }
+    }
 }

@@ -61,6 +61,8 @@ def lib():
         L.jko_row_norms.argtypes = [P, S, S, P]
         L.jko_gemv_fused.argtypes = [ctypes.c_int, P, S, S, P, S, P, ctypes.c_int]
         L.jko_max_threads.restype = ctypes.c_int
+        L.jko_quantize_act_q8.argtypes = [P, S, S, P, P, S]
+        L.jko_matmul_q8_int8.argtypes = [P, S, S, P, P, S, S, P, P]
         _lib = L
     return _lib
 
@@ -347,3 +349,37 @@ def q6k_transpose_f16(table: np.ndarray) -> np.ndarray:
 def softcap_f64(x: np.ndarray, cap: float) -> np.ndarray:
     """softcap (ops.rs:751-760): cap * tanh(x / cap)."""
     return np.float64(cap) * np.tanh(np.asarray(x, np.float64) / np.float64(cap))
+
+
+# ---------------------------------------------------------------------------------------------
+# The Q8_0 int8 path (the build's own definition; the reference only plans it,
+# docs/cubecl-int8-plan.md:48-60): per-32 activation quantization and the product of exact int32
+# block dots scaled in f32. Restated in jk_oracle.c.
+# ---------------------------------------------------------------------------------------------
+
+def q8_m_pad(m: int) -> int:
+    return (m + 3) // 4 * 4
+
+
+def quantize_act_q8(x: np.ndarray):
+    """x f32 [m, k] -> (xq int8 [m, k], xd f32 [k / 32, m_pad]) as jk_quantize_act_q8 defines them."""
+    x = np.ascontiguousarray(x, dtype=np.float32)
+    m, k = x.shape
+    mp = q8_m_pad(m)
+    xq = np.empty((m, k), np.int8)
+    xd = np.zeros((k // 32, mp), np.float32)
+    lib().jko_quantize_act_q8(_ptr(x), m, k, _ptr(xq), _ptr(xd), mp)
+    return xq, xd
+
+
+def matmul_q8_int8(raw: np.ndarray, n: int, k: int, xq: np.ndarray, xd: np.ndarray, with_dots: bool = False):
+    """The int8 product over raw Q8_0 rows (exact int32 block dots, f32 scaling in block order)."""
+    raw = np.ascontiguousarray(raw).view(np.uint8).reshape(-1)
+    xq = np.ascontiguousarray(xq, dtype=np.int8)
+    xd = np.ascontiguousarray(xd, dtype=np.float32)
+    m = xq.shape[0]
+    out = np.empty((m, n), np.float32)
+    dots = np.empty((m, n, k // 32), np.int32) if with_dots else None
+    lib().jko_matmul_q8_int8(_ptr(raw), n, k, _ptr(xq), _ptr(xd), m, xd.shape[1], _ptr(out),
+                             _ptr(dots) if with_dots else None)
+    return (out, dots) if with_dots else out

@@ -232,3 +232,38 @@ def test_head_oracle_follows_the_reference_test_definitions():
     got = oracle.pick_logits_f64(dense, x, [1, 4, 0, 60], 30.0)
     dot = float(np.dot(x[1].astype(np.float64), dense[4].astype(np.float64)))
     assert got[0] == pytest.approx(30.0 * np.tanh(dot / 30.0), rel=1e-12)
+
+
+# --- the Q8_0 int8 path's restatement (the build's definition; no reference implementation) -------
+
+def test_q8_activation_quantizer_restatement():
+    rng = np.random.default_rng(12)
+    x = (rng.standard_normal((7, 96)) * 2).astype(np.float32)
+    x[3, 32:64] = 0
+    xq, xd = oracle.quantize_act_q8(x)
+    assert xd.shape == (3, 8) and np.all(xd[:, 7] == 0)  # m_pad = 8: padding rows stay zero
+    assert np.all(xd[1, 3] == 0) and np.all(xq[3, 32:64] == 0)
+    d = np.repeat(xd[:, :7].T, 32, axis=1)                 # [m, k] scale of each element
+    assert np.all(np.abs(xq.astype(np.float32) * d - x) <= d / 2 * (1 + 1e-6))
+    assert np.abs(xq).max() == 127
+    amax = np.abs(x.reshape(7, 3, 32)).max(axis=2)
+    assert np.array_equal(xd[:, :7].T, (amax / np.float32(127)).astype(np.float32))
+
+
+def test_q8_int8_restatement_dots_and_order():
+    from jevons_kernels import synth
+    rng = np.random.default_rng(13)
+    n, k, m = 64, 128, 5
+    raw = synth.q8_0_blocks(rng, n, k)
+    x = rng.standard_normal((m, k)).astype(np.float32)
+    xq, xd = oracle.quantize_act_q8(x)
+    out, dots = oracle.matmul_q8_int8(raw, n, k, xq, xd, with_dots=True)
+    qw = raw.reshape(n * k // 32, 34)[:, 2:].view(np.int8).reshape(n, k // 32, 32).astype(np.int64)
+    want_dots = np.einsum("rbj,cbj->rcb", xq.reshape(m, k // 32, 32).astype(np.int64), qw)
+    assert np.array_equal(dots, want_dots)
+    dw = raw.reshape(n * k // 32, 34)[:, :2].copy().view(np.float16).astype(np.float32).reshape(n, k // 32)
+    acc = np.zeros((m, n), np.float32)
+    for b in range(k // 32):  # fma in block order == f64 product rounded once per block
+        s = (dw[None, :, b] * xd[b, :m][:, None]).astype(np.float32)
+        acc = (dots[:, :, b].astype(np.float64) * s.astype(np.float64) + acc.astype(np.float64)).astype(np.float32)
+    assert np.array_equal(out, acc)

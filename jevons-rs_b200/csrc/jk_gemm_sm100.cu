@@ -141,11 +141,12 @@ struct Smem {
     // CTA (NACC = 1) leaves room for two stages. A pair then decodes every weight tile once per
     // 256 activation rows and each SM's MMA (128 x 256 x 64 per k-block) outlasts its decoding.
     static constexpr bool TMEM_A = FMT != FMT_F16 && (PAIR ? BT == 256 : BT <= 128);
-    static constexpr int KPS = TMEM_A ? 4 : 1;                  // k-blocks per stage
+    static constexpr int KPS = TMEM_A ? 4 : 1;  // k-blocks per stage: one raw super-block
     static constexpr int B_ATOM = (PAIR ? BT / 2 : BT) * 128;  // one k-block of activations (a pair CTA: half the rows)
     static constexpr int B_STAGE = KPS * B_ATOM;
     static constexpr int raw_bytes = RawTile<FMT>::bytes;
     // accumulator buffers (the epilogue of one tile overlaps the MMAs of the next when there are 2)
+    // (one accumulator when two would leave fewer than two weight stages: the CTA pairs' 256 columns)
     static constexpr int NACC = TMEM_A && 2 * BT + 2 * 32 * KPS > 512 ? 1 : 2;
     static constexpr uint32_t TMEM_A0 = NACC * BT;  // first tensor-memory column of the A stages
     static constexpr Rings rings = TMEM_A ? pick_rings_tmem(B_STAGE, raw_bytes, (512 - NACC * BT) / (32 * KPS))

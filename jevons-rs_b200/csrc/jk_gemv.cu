@@ -98,18 +98,20 @@ __device__ __forceinline__ int dp2_16x8(uint32_t x2, uint32_t q4, int acc, bool 
     return hi ? __dp2a_hi((int)x2, (int)q4, acc) : __dp2a_lo((int)x2, (int)q4, acc);
 }
 
-// sum over 16 weights: 4 words of packed bytes (4 weights each) times 8 words of int16 pairs
+// sum over 16 weights: 4 words of packed bytes (4 weights each) times 8 words of int16 pairs, as
+// two independent dp2a chains (integer sums: the split changes no bit of the result, and halves
+// the dependent-instruction chain the warp waits on)
 __device__ __forceinline__ int dot16(const uint32_t (&q)[4], const uint4& xa, const uint4& xb) {
-    int acc = 0;
-    acc = dp2_16x8(xa.x, q[0], acc, false);
-    acc = dp2_16x8(xa.y, q[0], acc, true);
-    acc = dp2_16x8(xa.z, q[1], acc, false);
-    acc = dp2_16x8(xa.w, q[1], acc, true);
-    acc = dp2_16x8(xb.x, q[2], acc, false);
-    acc = dp2_16x8(xb.y, q[2], acc, true);
-    acc = dp2_16x8(xb.z, q[3], acc, false);
-    acc = dp2_16x8(xb.w, q[3], acc, true);
-    return acc;
+    int a0 = 0, a1 = 0;
+    a0 = dp2_16x8(xa.x, q[0], a0, false);
+    a1 = dp2_16x8(xa.y, q[0], a1, true);
+    a0 = dp2_16x8(xa.z, q[1], a0, false);
+    a1 = dp2_16x8(xa.w, q[1], a1, true);
+    a0 = dp2_16x8(xb.x, q[2], a0, false);
+    a1 = dp2_16x8(xb.y, q[2], a1, true);
+    a0 = dp2_16x8(xb.z, q[3], a0, false);
+    a1 = dp2_16x8(xb.w, q[3], a1, true);
+    return a0 + a1;
 }
 
 // Activation slot (step st, lane-in-row g, side h, 16-half) holding element e0 (a multiple of 16).

@@ -16,17 +16,19 @@
 //                       int8) TMA brings the weight tile, the activation tile and the 4 x 128
 //                       activation scales. The MMA warp issues ONE tcgen05.mma kind::i8 (K = 32)
 //                       per Q8_0 block into its own int32 accumulator (accumulate = 0), rotating
-//                       over four 128-column tensor-memory buffers, and commits each. Sixteen
-//                       rescale warps (4 per TMEM lane quarter, 32 activation columns each) read
-//                       a finished buffer with tcgen05.ld, free it, and fold it into f32
-//                       registers:  acc[c] = fma(f32(dot), f32(d_w[r, b]) * d_x[c, b], acc[c])
+//                       over four 128-column tensor-memory buffers, and commits each. Eight
+//                       rescale warps (2 per TMEM lane quarter, 64 activation columns each) read
+//                       a finished buffer with tcgen05.ld (two 32-column halves, one in flight
+//                       while the other is folded in), free it, and fold it into f32 registers:
+//                       acc[c] = fma(f32(dot), f32(d_w[r, b]) * d_x[c, b], acc[c])
 //                       in increasing block order. The int32 dots are exact (|dot| <= 32 * 127 *
 //                       127 < 2^24), so the product is bit-exact with a CPU restatement of the
 //                       same f32 operations.
 //
 // The CUDA cores, not the tensor pipe, bound this kernel: per 32-k block every accumulator
-// element costs a conversion, a multiply and an FMA (16384 elements per tile and block), while
-// the MMA of that block takes ~64 tensor cycles.
+// element costs an integer add and half a packed subtract (the int32 -> f32 conversion), half a
+// packed multiply (the scale product) and half a packed FMA, 16384 elements per tile and block,
+// while the MMA of that block takes ~64 tensor cycles.
 #include "jk_internal.h"
 
 #include <cuda_bf16.h>
@@ -46,7 +48,8 @@ constexpr int I8_S_BYTES = 4 * I8_BT * 4;   // 2 KB: activation scales of the st
 constexpr int I8_STAGE = I8_W_BYTES + I8_X_BYTES + I8_S_BYTES;
 constexpr int I8_STAGES = 6;
 constexpr int I8_NBUF = 4;                  // int32 accumulators of 128 columns: all of TMEM
-constexpr int I8_RS_WARPS = 16;             // rescale warps 4..19
+constexpr int I8_RS_WARPS = 8;              // rescale warps 4..11: 2 per TMEM lane quarter
+constexpr int I8_COLS = I8_BT / 2;          // activation columns per rescale warp
 constexpr int I8_RS_WARP0 = 4;
 constexpr int I8_THREADS = 32 * (I8_RS_WARP0 + I8_RS_WARPS);
 constexpr int I8_OFF_BAR = I8_STAGES * I8_STAGE;
@@ -71,6 +74,31 @@ __device__ __forceinline__ void mma_i8(uint32_t d_tmem, uint64_t a_desc, uint64_
 
 __device__ __forceinline__ void gdc_launch_i8() { asm volatile("griddepcontrol.launch_dependents;" ::: "memory"); }
 __device__ __forceinline__ void gdc_wait_i8() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
+
+// acc[C0 + c] = fma(f32(v[c]), dw * sx[C0 + c], acc[C0 + c]) for c < 32, in packed f32x2 arithmetic.
+// int32 -> f32 without the conversion unit: |v| < 2^22, so the bits of 1.5 * 2^23 + v are those of
+// 0x4B400000 + v and one exact subtraction leaves v.
+template <int C0 = 0>
+__device__ __forceinline__ void rescale32(float (&acc)[I8_COLS], const uint32_t (&v)[32], float dw, const float* sx) {
+    const float2 dw2 = make_float2(dw, dw), magic = make_float2(12582912.0f, 12582912.0f);
+    const float4* s4 = reinterpret_cast<const float4*>(sx + C0);
+#pragma unroll
+    for (int q = 0; q < 8; ++q) {
+        const float4 d4 = s4[q];
+        const float2 sa = mul2(dw2, make_float2(d4.x, d4.y));
+        const float2 sb = mul2(dw2, make_float2(d4.z, d4.w));
+        const float2 fa = sub2(make_float2(__int_as_float(0x4B400000 + (int)v[4 * q]),
+                                           __int_as_float(0x4B400000 + (int)v[4 * q + 1])), magic);
+        const float2 fb = sub2(make_float2(__int_as_float(0x4B400000 + (int)v[4 * q + 2]),
+                                           __int_as_float(0x4B400000 + (int)v[4 * q + 3])), magic);
+        const float2 ra = fma2(fa, sa, make_float2(acc[C0 + 4 * q], acc[C0 + 4 * q + 1]));
+        const float2 rb = fma2(fb, sb, make_float2(acc[C0 + 4 * q + 2], acc[C0 + 4 * q + 3]));
+        acc[C0 + 4 * q] = ra.x;
+        acc[C0 + 4 * q + 1] = ra.y;
+        acc[C0 + 4 * q + 2] = rb.x;
+        acc[C0 + 4 * q + 3] = rb.y;
+    }
+}
 
 struct I8Sched {
     int64_t tiles, tiles_m;
@@ -187,66 +215,76 @@ gemm_i8_kernel(const __grid_constant__ CUtensorMap tm_w, const __grid_constant__
         }
     } else if (warp >= I8_RS_WARP0) {
         // ------------------------------ rescale warps ------------------------------
+        // Warp 4 + i reads TMEM lanes 32 (i % 4) .. (its weight rows) and activation columns
+        // 64 (i / 4) .. of every block accumulator, as two 32-column halves H0 / H1 held in vA / vB.
+        // Software pipeline: the load of one half is in flight while the other half is folded in,
+        // so the tensor-memory load latency and the next block's barrier wait overlap arithmetic.
         const int i = warp - I8_RS_WARP0;
-        const int quarter = warp & 3;             // TMEM lanes this warp may read: 32 quarter ..
-        const int cgrp = i >> 2;                  // activation columns 32 cgrp ..
+        const int quarter = warp & 3;
+        const int cgrp = i >> 2;
         const int row_in_tile = 32 * quarter + lane;
-        const uint32_t tbase = tmem + ((uint32_t)(32 * quarter) << 16) + (uint32_t)(32 * cgrp);
+        const uint32_t tbase = tmem + ((uint32_t)(32 * quarter) << 16) + (uint32_t)(I8_COLS * cgrp);
         int it = 0, g = 0;
+        uint32_t vA[32], vB[32];
         for (int64_t t = blockIdx.x; t < sc.tiles && ok; t += G) {
             const int64_t wrow = (t / sc.tiles_m) * I8_BW + row_in_tile;
-            const int64_t m0 = (t % sc.tiles_m) * I8_BT + 32 * cgrp;
+            const int64_t m0 = (t % sc.tiles_m) * I8_BT + I8_COLS * cgrp;
             const bool row_ok = wrow < w.rows;
             const uint16_t* dw_row = w.d + (row_ok ? wrow : 0) * (int64_t)sc.nblk;
-            float acc[32];
+            float acc[I8_COLS];
 #pragma unroll
-            for (int c = 0; c < 32; ++c) acc[c] = 0.f;
-            for (int ks = 0; ks < sc.kst && ok; ++ks, ++it) {
-                const int s = it % I8_STAGES;
-                // the stage's activation scales (TMA) are visible after its full phase
-                ok = __all_sync(0xFFFFFFFFu, mbar_wait(full(s), (it / I8_STAGES) & 1, err));
-                if (!ok) break;
-                const int nb = sc.nblk - 4 * ks < 4 ? sc.nblk - 4 * ks : 4;
-                uint16_t dwh[4] = {0, 0, 0, 0};
-                for (int j = 0; j < nb; ++j) dwh[j] = __ldg(dw_row + 4 * ks + j);
-                const float* sx = reinterpret_cast<const float*>(smem + s * I8_STAGE + I8_W_BYTES + I8_X_BYTES) + 32 * cgrp;
-                for (int j = 0; j < nb && ok; ++j, ++g) {
-                    const int b = g % I8_NBUF;
-                    ok = __all_sync(0xFFFFFFFFu, mbar_wait(acc_full(b), (g / I8_NBUF) & 1, err));
+            for (int c = 0; c < I8_COLS; ++c) acc[c] = 0.f;
+            // prologue: H0 of the tile's first block
+            ok = __all_sync(0xFFFFFFFFu, mbar_wait(acc_full(g % I8_NBUF), (g / I8_NBUF) & 1, err));
+            if (!ok) break;
+            tc_fence_after();
+            tmem_ld32(tbase + (uint32_t)((g % I8_NBUF) * I8_BT), vA);
+            tmem_ld_wait();
+            uint32_t dwp0 = 0, dwp1 = 0;  // the row's 4 f16 block scales of the current stage
+            const float* sx = nullptr;
+            for (int bl = 0; bl < sc.nblk; ++bl, ++g) {
+                const int ks = bl >> 2, j = bl & 3;
+                const int s = (it + ks) % I8_STAGES;
+                if (j == 0) {
+                    // the stage's activation scales (TMA) are visible after its full phase
+                    ok = __all_sync(0xFFFFFFFFu, mbar_wait(full(s), ((it + ks) / I8_STAGES) & 1, err));
+                    if (!ok) break;
+                    const uint16_t* dp = dw_row + 4 * ks;
+                    const int nb = sc.nblk - 4 * ks;
+                    dwp0 = nb >= 2 ? __ldg(reinterpret_cast<const uint32_t*>(dp)) : (uint32_t)__ldg(dp);
+                    dwp1 = nb >= 4 ? __ldg(reinterpret_cast<const uint32_t*>(dp) + 1) : nb == 3 ? (uint32_t)__ldg(dp + 2) : 0u;
+                    sx = reinterpret_cast<const float*>(smem + s * I8_STAGE + I8_W_BYTES + I8_X_BYTES) + I8_COLS * cgrp;
+                }
+                const uint32_t b = (uint32_t)(g % I8_NBUF);
+                const float dw = half_bits_to_float(((j < 2 ? dwp0 : dwp1) >> (16 * (j & 1))) & 0xFFFFu);
+                const float* sxj = sx + j * I8_BT;
+                tmem_ld32(tbase + b * I8_BT + 32, vB);            // H1 of this block, in flight ...
+                rescale32(acc, vA, dw, sxj);                       // ... while H0 is folded in
+                tmem_ld_wait();
+                tc_fence_before();
+                __syncwarp();
+                if (lane == 0) mbar_arrive(acc_empty(b));          // both halves are in registers
+                const bool more = bl + 1 < sc.nblk;
+                if (more) {
+                    const int gn = g + 1;
+                    ok = __all_sync(0xFFFFFFFFu, mbar_wait(acc_full(gn % I8_NBUF), (gn / I8_NBUF) & 1, err));
                     if (!ok) break;
                     tc_fence_after();
-                    uint32_t v[32];
-                    tmem_ld32(tbase + (uint32_t)(b * I8_BT), v);
-                    tmem_ld_wait();
-                    tc_fence_before();
-                    __syncwarp();
-                    if (lane == 0) mbar_arrive(acc_empty(b));
-                    const float dw = half_bits_to_float(dwh[j]);
-                    const float2 dw2 = make_float2(dw, dw);
-                    const float4* s4 = reinterpret_cast<const float4*>(sx + j * I8_BT);
-#pragma unroll
-                    for (int q = 0; q < 8; ++q) {
-                        const float4 d4 = s4[q];
-                        const float2 sa = mul2(dw2, make_float2(d4.x, d4.y));
-                        const float2 sb = mul2(dw2, make_float2(d4.z, d4.w));
-                        const float2 fa = make_float2(__int2float_rn((int)v[4 * q]), __int2float_rn((int)v[4 * q + 1]));
-                        const float2 fb = make_float2(__int2float_rn((int)v[4 * q + 2]), __int2float_rn((int)v[4 * q + 3]));
-                        const float2 ra = fma2(fa, sa, make_float2(acc[4 * q], acc[4 * q + 1]));
-                        const float2 rb = fma2(fb, sb, make_float2(acc[4 * q + 2], acc[4 * q + 3]));
-                        acc[4 * q] = ra.x;
-                        acc[4 * q + 1] = ra.y;
-                        acc[4 * q + 2] = rb.x;
-                        acc[4 * q + 3] = rb.y;
-                    }
+                    tmem_ld32(tbase + (uint32_t)((gn % I8_NBUF) * I8_BT), vA);  // next block's H0 ...
                 }
-                __syncwarp();
-                if (lane == 0) mbar_arrive(empty(s));  // done with the stage's scales
+                rescale32<32>(acc, vB, dw, sxj);                   // ... while H1 is folded in
+                if (more) tmem_ld_wait();
+                if (j == 3 || !more) {
+                    __syncwarp();
+                    if (lane == 0) mbar_arrive(empty(s));           // done with the stage's scales
+                }
             }
             if (!ok) break;
+            it += sc.kst;
             if (row_ok) {
                 float* o = out + m0 * ldo + wrow;
 #pragma unroll
-                for (int c = 0; c < 32; ++c)
+                for (int c = 0; c < I8_COLS; ++c)
                     if (m0 + c < m) o[c * ldo] = acc[c];
             }
         }

@@ -9,7 +9,7 @@
 // B200 design: the exchange uses the copy engines, not SMs. The persistent tensor-core product
 // holds every SM, so a collective kernel (NCCL's all-gather) can only run between products; copy
 // engines push each finished row chunk of this rank's shard straight into every peer's buffer
-// (cudaMemcpyAsync to peer memory mapped with CUDA IPC, one copy stream per peer) while the next
+// (cudaMemcpyAsync to peer memory mapped with CUDA IPC, NSUB copy streams per peer) while the next
 // chunk's product runs. After its last copies a rank increments its counter word in every peer
 // (flags[rank] += 1, a system-scope release reduction by a one-thread kernel ordered after the
 // copies on each copy stream). Each rank's own slot flags[rank] counts the calls it has waited
@@ -30,6 +30,9 @@ namespace {
 
 constexpr int MAX_WORLD = 8;
 constexpr int MAX_CHUNKS = 16;
+// Copy streams per peer: one copy engine moves a few-MB peer copy at a fraction of the link rate,
+// so each chunk's copy to a peer is split in NSUB row ranges on NSUB streams (engines).
+constexpr int NSUB = 4;
 constexpr uint64_t FLAG_WAIT_NS = 2000000000ull;  // 2 s
 
 // peer_flags[rank] += 1 in a peer's flag array, after this stream's copies to that peer
@@ -64,10 +67,11 @@ __global__ void wait_peers_kernel(uint32_t* flags, int world, int rank, uint32_t
     if (p == 0) flags[rank] = target;
 }
 
-// Copy streams (one per peer) and events, created once per device.
+// Copy streams (NSUB per peer) and events, created once per device.
 struct ShardState {
     bool ready = false;
-    cudaStream_t cs[MAX_WORLD] = {};
+    cudaStream_t cs[MAX_WORLD][NSUB] = {};
+    cudaEvent_t sub[MAX_WORLD][NSUB] = {};
     cudaEvent_t chunk[MAX_CHUNKS] = {};
     cudaEvent_t done[MAX_WORLD] = {};
 };
@@ -80,8 +84,11 @@ jk_status shard_state(int device, ShardState** out) {
     ShardState& s = st[device];
     if (!s.ready) {
         for (int p = 0; p < MAX_WORLD; ++p) {
-            cudaError_t e = cudaStreamCreateWithFlags(&s.cs[p], cudaStreamNonBlocking);
-            if (e == cudaSuccess) e = cudaEventCreateWithFlags(&s.done[p], cudaEventDisableTiming);
+            cudaError_t e = cudaEventCreateWithFlags(&s.done[p], cudaEventDisableTiming);
+            for (int q = 0; q < NSUB && e == cudaSuccess; ++q) {
+                e = cudaStreamCreateWithFlags(&s.cs[p][q], cudaStreamNonBlocking);
+                if (e == cudaSuccess) e = cudaEventCreateWithFlags(&s.sub[p][q], cudaEventDisableTiming);
+            }
             if (e != cudaSuccess) return cuda_fail(e, "sharded product: copy stream set-up");
         }
         for (int i = 0; i < MAX_CHUNKS; ++i) {
@@ -199,20 +206,32 @@ extern "C" jk_status jk_sharded_matmul_allgather(const jk_qmatrix* w_shard, cons
         cudaError_t e = cudaEventRecord(ss->chunk[i], cs);
         for (int p = 0; p < world && e == cudaSuccess; ++p) {
             if (p == rank) continue;
-            e = cudaStreamWaitEvent(ss->cs[p], ss->chunk[i], 0);
-            if (e == cudaSuccess)
-                e = cudaMemcpyAsync(out_peers[p] + (size_t)rank * m * n_r + r0 * n_r, mine + r0 * n_r, rows * n_r * 4,
-                                    cudaMemcpyDeviceToDevice, ss->cs[p]);
+            for (int q = 0; q < jk::NSUB && e == cudaSuccess; ++q) {
+                const size_t q0 = r0 + rows * q / jk::NSUB, q1 = r0 + rows * (q + 1) / jk::NSUB;
+                if (q1 <= q0) continue;
+                e = cudaStreamWaitEvent(ss->cs[p][q], ss->chunk[i], 0);
+                if (e == cudaSuccess)
+                    e = cudaMemcpyAsync(out_peers[p] + (size_t)rank * m * n_r + q0 * n_r, mine + q0 * n_r,
+                                        (q1 - q0) * n_r * 4, cudaMemcpyDeviceToDevice, ss->cs[p][q]);
+            }
         }
         if (e != cudaSuccess) return jk::cuda_fail(e, "sharded product: chunk copies");
     }
     if (world == 1) return JK_OK;
     for (int p = 0; p < world; ++p) {
         if (p == rank) continue;
-        // on peer p's copy stream, after this call's copies to p: flags_peers[p][rank] += 1
-        jk::signal_peer_kernel<<<1, 32, 0, ss->cs[p]>>>(flags_peers[p] + rank);
-        cudaError_t e = cudaGetLastError();
-        if (e == cudaSuccess) e = cudaEventRecord(ss->done[p], ss->cs[p]);
+        // peer p's first copy stream joins the others, then, after this call's copies to p:
+        // flags_peers[p][rank] += 1
+        cudaError_t e = cudaSuccess;
+        for (int q = 1; q < jk::NSUB && e == cudaSuccess; ++q) {
+            e = cudaEventRecord(ss->sub[p][q], ss->cs[p][q]);
+            if (e == cudaSuccess) e = cudaStreamWaitEvent(ss->cs[p][0], ss->sub[p][q], 0);
+        }
+        if (e == cudaSuccess) {
+            jk::signal_peer_kernel<<<1, 32, 0, ss->cs[p][0]>>>(flags_peers[p] + rank);
+            e = cudaGetLastError();
+        }
+        if (e == cudaSuccess) e = cudaEventRecord(ss->done[p], ss->cs[p][0]);
         if (e != cudaSuccess) return jk::cuda_fail(e, "sharded product: peer signal");
     }
     if (wait) return jk_allgather_wait(w_shard->device, flags_peers[rank], world, rank, 1, stream);

@@ -293,6 +293,72 @@ def grouped_bench(gpu, dev, timed, pk):
             "workloads": results}
 
 
+# BASELINE config 3 (crates/jevons-parakeet/src/config.rs:183-186, encoder.rs:53-61): 24 encoder
+# layers of Q8_0 linears at M=750 frames, d=1024: FFN 1024->4096->1024 and four 1024->1024
+# attention projections; each linear gets its own seeded f32 N(0,1) input (not chained).
+CFG3_M, CFG3_D, CFG3_FF, CFG3_LAYERS = 750, 1024, 4096, 24
+CFG3_SHAPES = [(CFG3_FF, CFG3_D), (CFG3_D, CFG3_FF)] + [(CFG3_D, CFG3_D)] * 4  # (n, k) per linear
+
+
+def int8_peak_tops(dev):
+    """Dense int8 tensor peak measured here: torch._int_mm (cuBLASLt) on 8192^3, best of 10."""
+    import torch
+    a = torch.randint(-128, 127, (8192, 8192), dtype=torch.int8, device=dev)
+    b = torch.randint(-128, 127, (8192, 8192), dtype=torch.int8, device=dev)
+    for _ in range(3):
+        torch._int_mm(a, b.t())
+    torch.cuda.synchronize()
+    best = 1e9
+    for _ in range(10):
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record()
+        torch._int_mm(a, b.t())
+        e1.record()
+        torch.cuda.synchronize()
+        best = min(best, e0.elapsed_time(e1))
+    return 2.0 * 8192 ** 3 / (best * 1e-3) / 1e12
+
+
+def cfg3_bench(gpu, dev, timed, pk, scratch):
+    """Config 3, one step = one pass over the 24 layers x 6 linears (144 products, 320 MB of Q8_0
+    weights): the int8 path (jk_quantize_act_q8 + jk_matmul_q8_int8 per linear) and the bf16
+    tensor-core path (jk_matmul on the f32 activations, rounded to bf16), CUDA graph replay."""
+    import torch
+    from jevons_kernels import synth
+    from jevons_kernels.gemm import Buf, QMatrix, matmul, matmul_q8_int8, q8_scales_len, quantize_act_q8
+    m = CFG3_M
+    rng = np.random.default_rng(3)
+    raws = {shape: synth.q8_0_blocks(rng, shape[0], shape[1]) for shape in set(CFG3_SHAPES)}
+    ws = [QMatrix.upload(gpu, 8, n, k, 1, raws[(n, k)]) for _ in range(CFG3_LAYERS) for (n, k) in CFG3_SHAPES]
+    xs = {k: torch.from_numpy(synth.activations(np.random.default_rng(30 + k), m, k)).to(dev) for k in (CFG3_D, CFG3_FF)}
+    xq = {k: torch.empty(m * k, dtype=torch.int8, device=dev) for k in xs}
+    xd = {k: torch.empty(q8_scales_len(m, k), device=dev) for k in xs}
+    outs = [torch.empty(m, w_n, device=dev) for w_n in (CFG3_FF, CFG3_D)]
+    lin = [(ws[i], CFG3_SHAPES[i % 6]) for i in range(len(ws))]
+
+    def step_i8():
+        for w, (n, k) in lin:
+            quantize_act_q8(gpu, Buf(xs[k]), m, k, Buf(xq[k]), Buf(xd[k]))
+            matmul_q8_int8(gpu, w, Buf(xq[k]), Buf(xd[k]), m, Buf(outs[0 if n == CFG3_FF else 1]))
+
+    def step_bf16():
+        for w, (n, k) in lin:
+            matmul(gpu, Buf(xs[k]), m, w, Buf(outs[0 if n == CFG3_FF else 1]), None, scratch)
+    steps = 10
+    flops = sum(2.0 * m * n * k for _, (n, k) in lin)
+    t_i8 = timed(step_i8, steps, 3) / steps
+    t_bf = timed(step_bf16, steps, 3) / steps
+    peak_i8 = int8_peak_tops(dev)
+    v_i8, v_bf = flops / (t_i8 * 1e-3) / 1e12, flops / (t_bf * 1e-3) / 1e12
+    return {"what": "BASELINE config 3: 24 x {1024->4096, 4096->1024, 4 x 1024->1024} Q8_0 linears at M=750, "
+                    "f32 activations; one step = all 144 products; CUDA graph replay, CUDA events",
+            "int8_path": {"ms_per_step": t_i8, "tops": v_i8, "peak_int8_tops": peak_i8, "frac_of_int8_peak": v_i8 / peak_i8,
+                          "includes": "per-linear activation quantization + kind::i8 product"},
+            "bf16_path": {"ms_per_step": t_bf, "tflops": v_bf, "peak_bf16_tflops": pk.get("bf16_tflops"),
+                          "frac_of_bf16_peak": v_bf / pk.get("bf16_tflops", 1.0), "includes": "f32->bf16 conversion + product"},
+            "faster": "int8" if t_i8 < t_bf else "bf16"}
+
+
 HEAD_VOCAB = 262144  # token-table rows of the head workloads (the Gemma vocabulary)
 
 
@@ -437,7 +503,7 @@ def run_ours(args):
         if world > 1:
             for i in range(L):
                 pg.run(ws[i], x, i=i, wait=False, chunks=1, scratch=scratch)
-            pg.wait(L)
+            pg.wait()
         else:
             for i in range(L):
                 matmul(gpu, xbuf, M_ROWS, ws[i], obufs[i], None, scratch)
@@ -598,10 +664,10 @@ def run_ours(args):
 
         def head_compute():
             matmul(gpu, xvb, mv, w4, ovb, None, scratch)
-        c_ms = timed(head_compute, v_steps, 3) / v_steps
+        hc_ms = timed(head_compute, v_steps, 3) / v_steps
         flops_v = 2.0 * mv * VOCAB_N * K_DIM
         vplan = Plan.heuristic(w4, mv, False)
-        e_v_ms = c_ms
+        e_v_ms = hc_ms
         if world > 1:
             del ov, ovb
             pgv = PeerGather(gpu, mv, n_r, buffers=1)
@@ -616,13 +682,18 @@ def run_ours(args):
                          f"{world} GPU(s), f32 logits all-gathered by copy engines (jk_sharded_matmul_allgather, "
                          f"{VOCAB_CHUNKS} row chunks); CUDA graph replay, CUDA events, max over ranks",
                  "plan": repr(vplan), "n_per_gpu": n_r,
-                 "compute_ms": c_ms, "compute_tflops_total": flops_v / (c_ms * 1e-3) / 1e12,
+                 "compute_ms": hc_ms, "compute_tflops_total": flops_v / (hc_ms * 1e-3) / 1e12,
                  "e2e_ms": e_v_ms, "e2e_tflops_total": flops_v / (e_v_ms * 1e-3) / 1e12,
                  "gather_bytes_sent_per_gpu": gather_bytes,
                  "roofline": {"compute_ms": t_comp, "nvlink_ms": t_link, "bound": "nvlink" if t_link > t_comp else "tensor",
                               "frac": max(t_comp, t_link) / e_v_ms, "nvlink_gbs": NVLINK_GBS,
                               "peak_tflops": pk.get("bf16_tflops")}}
         del w4
+
+    # ---- Parakeet encoder linears on Q8_0, int8 path and bf16 path ---------
+    cfg3 = None
+    if world == 1 and not args.no_cfg3:
+        cfg3 = cfg3_bench(gpu, dev, timed, pk, scratch)
 
     # ---- expert-grouped products (the reference's routed workloads), one GPU only -------------
     grouped = None
@@ -669,9 +740,10 @@ def run_ours(args):
                     "value": f16_tflops, "unit": "TFLOP/s", "ms_per_step": f16_ms / args.steps},
             "gemv_vocab": gv4,
             "vocab_head": vocab,
+            "cfg3_parakeet_q8_0": cfg3,
             # per step: one tensor-core kernel per layer; with N GPUs also one signal kernel per peer
-            # and layer (on the copy streams) and one wait kernel
-            "gpu_launches": args.steps * (L * launches_per_product + ((world - 1) * L + 1 if world > 1 else 0)),
+            # (on the copy streams) and one wait kernel
+            "gpu_launches": args.steps * (L * launches_per_product + (world if world > 1 else 0)),
             "timing": "CUDA graph replay of each step, CUDA events, max over ranks",
             "clocks": sampler.report(),
             "cpu_baseline": cpu,
@@ -695,6 +767,7 @@ def main():
     ap.add_argument("--no-grouped", action="store_true", help="skip the expert-grouped workloads")
     ap.add_argument("--no-head", action="store_true", help="skip the Q6_K embedding-table workloads")
     ap.add_argument("--no-vocab", action="store_true", help="skip config 4's head (M=1 and M=2048, sharded)")
+    ap.add_argument("--no-cfg3", action="store_true", help="skip config 3 (Q8_0 Parakeet linears, int8 and bf16 paths)")
     ap.add_argument("--head-only", action="store_true", help="run only the Q6_K embedding-table workloads")
     ap.add_argument("--head-vocab", type=int, default=HEAD_VOCAB, help="table rows of the head workloads")
     args = ap.parse_args()

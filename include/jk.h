@@ -308,28 +308,27 @@ jk_status jk_ipc_close(int device, void *dev_ptr);
  * row chunks (1..16, multiples of 32 rows) into this rank's block of its own buffer; each finished
  * chunk is pushed into every peer's buffer by the copy engines (one copy stream per peer, inside
  * the library) while the next chunk's product runs, so the exchange takes no SMs from the product.
- * After its copies the rank adds one to flags_peers[p][rank] in every peer (a system-scope
- * reduction ordered after the copies); a rank's own slot flags[rank] counts the calls it has
- * waited for. With wait != 0, `stream` then joins this rank's copies and a one-warp kernel waits
- * until every peer's counter has reached this call (every peer's shard has landed): the gathered
- * output is complete on `stream` after the call. With wait == 0 the call returns with the copies
- * still running beside `stream` (the next product can overlap them): this rank's block of
- * out_peers[rank] must then stay untouched, and the caller ends the exchange with
- * jk_allgather_wait(..., calls, ...) for the `calls` products made with these flags since the
- * last wait (for example once after several layers, each with its own output buffers). All ranks
- * make the same calls in the same order. The counters live on the device, so a captured CUDA graph
- * that replays these calls stays in step. Waits are bounded (2 s): a peer that never signals sets
- * ERR_WAIT_TIMEOUT, read with jk_device_error. A result stays valid until the next call on any
- * rank that writes the same buffers. Inside a CUDA graph capture, jk_allgather_wait joins copies
- * issued in the same capture only. */
+ * The copy streams carry copies only (a kernel there would wait for an SM the products hold). With
+ * wait != 0 the call ends with jk_allgather_wait: the gathered output is complete on `stream`
+ * after it. With wait == 0 the call returns with its copies still running beside `stream` (the
+ * next product can overlap them): this rank's block of out_peers[rank] must then stay untouched
+ * until the caller's next jk_allgather_wait, which covers every copy issued since the previous
+ * wait (for example once after several layers, each with its own output buffers). All ranks make
+ * the same calls and waits in the same order. A result stays valid until the next call on any
+ * rank that writes the same buffers. */
 jk_status jk_sharded_matmul_allgather(const jk_qmatrix *w_shard, const void *x, int x_dtype, size_t x_len,
                                       size_t m, int rank, int world, float *const *out_peers,
                                       uint32_t *const *flags_peers, int chunks, int wait,
                                       jk_split_scratch *scratch, void *stream);
-/* Joins this rank's outstanding copies on `stream`, then waits until every peer's counter in
- * flags (this rank's flag words) has reached flags[rank] + calls, and advances flags[rank]
- * (bounded, as above). */
-jk_status jk_allgather_wait(int device, uint32_t *flags, int world, int rank, uint32_t calls, void *stream);
+/* Ends an exchange: after all copies this rank issued since its previous wait, adds one to
+ * flags_peers[p][rank] in every peer p (a system-scope reduction ordered after those copies),
+ * joins the copy streams into `stream`, and waits on `stream` (one warp) until every peer's counter
+ * in this rank's flags has reached flags[rank] + 1, then advances flags[rank] (this rank's count of
+ * waits). The counters live on the device, so a captured CUDA graph that replays calls and waits
+ * stays in step with the peers. Bounded (2 s): a peer that never signals sets ERR_WAIT_TIMEOUT,
+ * read with jk_device_error. Inside a CUDA graph capture, call it after at least one product of
+ * the same capture. */
+jk_status jk_allgather_wait(int device, uint32_t *const *flags_peers, int world, int rank, void *stream);
 
 /* ---- allocation-free product ----------------------------------------------------------------- */
 

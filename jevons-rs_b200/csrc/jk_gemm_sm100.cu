@@ -93,6 +93,11 @@ struct RawTile {
 
 constexpr int SMEM_LIMIT = 227 * 1024;
 
+// The fewest tensor-memory weight stages a tile configuration keeps two accumulator buffers for.
+#ifndef JK_MIN_TMEM_STAGES
+#define JK_MIN_TMEM_STAGES 2
+#endif
+
 // Stage counts. Quantized weights use three rings: SX activation tiles (TMA), SA dequantized weight
 // tiles, R raw super-blocks (TMA). The activation ring is decoupled from the weight ring so that
 // several activation tiles are in flight (their L2 latency is the longest in the loop) while the
@@ -146,8 +151,8 @@ struct Smem {
     static constexpr int B_STAGE = KPS * B_ATOM;
     static constexpr int raw_bytes = RawTile<FMT>::bytes;
     // accumulator buffers (the epilogue of one tile overlaps the MMAs of the next when there are 2)
-    // (one accumulator when two would leave fewer than two weight stages: the CTA pairs' 256 columns)
-    static constexpr int NACC = TMEM_A && 2 * BT + 2 * 32 * KPS > 512 ? 1 : 2;
+    // (one accumulator when two would leave fewer than JK_MIN_TMEM_STAGES weight stages)
+    static constexpr int NACC = TMEM_A && 2 * BT + JK_MIN_TMEM_STAGES * 32 * KPS > 512 ? 1 : 2;
     static constexpr uint32_t TMEM_A0 = NACC * BT;  // first tensor-memory column of the A stages
     static constexpr Rings rings = TMEM_A ? pick_rings_tmem(B_STAGE, raw_bytes, (512 - NACC * BT) / (32 * KPS))
                                           : pick_rings(B_STAGE, raw_bytes);

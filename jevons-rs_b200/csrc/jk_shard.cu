@@ -10,13 +10,15 @@
 // holds every SM, so a collective kernel (NCCL's all-gather) can only run between products; copy
 // engines push each finished row chunk of this rank's shard straight into every peer's buffer
 // (cudaMemcpyAsync to peer memory mapped with CUDA IPC, NSUB copy streams per peer) while the next
-// chunk's product runs. After its last copies a rank increments its counter word in every peer
-// (flags[rank] += 1, a system-scope release reduction by a one-thread kernel ordered after the
-// copies on each copy stream). Each rank's own slot flags[rank] counts the calls it has waited
-// for: the receiving rank's wait kernel (one warp) polls its flags with system-scope acquires
-// until every peer's counter reaches flags[rank] + calls, then advances flags[rank]. The counters
-// live on the device, so a CUDA graph that replays a captured step stays in step with the peers
-// (no host-side epoch is baked into the graph). Every wait is bounded (2 s):
+// chunk's product runs. The copy streams carry copies only: a kernel there would wait for an SM
+// the persistent products hold. A wait (jk_allgather_wait, or a call with wait != 0) then
+// increments this rank's counter word in every peer (flags[rank] += 1, a system-scope release
+// reduction by a one-thread kernel ordered after all copies issued to that peer since the last
+// wait) and polls its own flags: each rank's own slot flags[rank] counts the waits it has done,
+// and the wait kernel (one warp) waits with system-scope acquires until every peer's counter
+// reaches flags[rank] + 1, then advances flags[rank]. The counters live on the device, so a CUDA
+// graph that replays a captured step stays in step with the peers (no host-side epoch is baked
+// into the graph). Every wait is bounded (2 s):
 // on expiry the kernel records ERR_WAIT_TIMEOUT in the device error word and returns, so a rank
 // that never arrives surfaces as an error instead of a hung GPU.
 #include "jk_internal.h"
@@ -43,11 +45,11 @@ __global__ void signal_peer_kernel(uint32_t* word) {
     }
 }
 
-// Waits until flags[p] >= flags[rank] + calls for every peer p (each peer's counter of signals),
-// then advances flags[rank], this rank's count of calls waited for. One warp, lane p polls peer p.
-__global__ void wait_peers_kernel(uint32_t* flags, int world, int rank, uint32_t calls, uint32_t* err) {
+// Waits until flags[p] >= flags[rank] + 1 for every peer p (each peer's counter of signals), then
+// advances flags[rank], this rank's count of waits. One warp, lane p polls peer p.
+__global__ void wait_peers_kernel(uint32_t* flags, int world, int rank, uint32_t* err) {
     const int p = threadIdx.x;
-    const uint32_t target = flags[rank] + calls;  // only this rank writes its own slot
+    const uint32_t target = flags[rank] + 1;  // only this rank writes its own slot
     bool ok = true;
     if (p < world && p != rank) {
         const uint64_t t0 = globaltimer();
@@ -146,24 +148,36 @@ extern "C" jk_status jk_ipc_close(int device, void* dev_ptr) {
     return jk::cuda_fail(cudaIpcCloseMemHandle(dev_ptr), "ipc close");
 }
 
-extern "C" jk_status jk_allgather_wait(int device, uint32_t* flags, int world, int rank, uint32_t calls,
-                                       void* stream) {
+extern "C" jk_status jk_allgather_wait(int device, uint32_t* const* flags_peers, int world, int rank, void* stream) {
     if (world < 1 || world > jk::MAX_WORLD || rank < 0 || rank >= world)
         return fail(JK_ERR_INVALID, "allgather wait: rank / world out of range (world <= 8)");
     if (world == 1) return JK_OK;
-    if (!flags) return fail(JK_ERR_INVALID, "allgather wait: null flags");
+    if (!flags_peers) return fail(JK_ERR_INVALID, "allgather wait: null flag table");
+    for (int p = 0; p < world; ++p)
+        if (!flags_peers[p]) return fail(JK_ERR_INVALID, "allgather wait: null flags");
     jk::DeviceGuard g(device);
     jk::ShardState* ss = nullptr;
     jk_status st = jk::shard_state(device, &ss);
     if (st != JK_OK) return st;
     cudaStream_t cs = static_cast<cudaStream_t>(stream);
-    // join this rank's outgoing copies (each peer stream's latest signal covers all its earlier work)
     for (int p = 0; p < world; ++p) {
         if (p == rank) continue;
-        cudaError_t e = cudaStreamWaitEvent(cs, ss->done[p], 0);
-        if (e != cudaSuccess) return jk::cuda_fail(e, "allgather wait: join copies");
+        // peer p's first copy stream joins the others; after every copy issued to p since the last
+        // wait: flags_peers[p][rank] += 1; then `stream` joins that stream
+        cudaError_t e = cudaSuccess;
+        for (int q = 1; q < jk::NSUB && e == cudaSuccess; ++q) {
+            e = cudaEventRecord(ss->sub[p][q], ss->cs[p][q]);
+            if (e == cudaSuccess) e = cudaStreamWaitEvent(ss->cs[p][0], ss->sub[p][q], 0);
+        }
+        if (e == cudaSuccess) {
+            jk::signal_peer_kernel<<<1, 32, 0, ss->cs[p][0]>>>(flags_peers[p] + rank);
+            e = cudaGetLastError();
+        }
+        if (e == cudaSuccess) e = cudaEventRecord(ss->done[p], ss->cs[p][0]);
+        if (e == cudaSuccess) e = cudaStreamWaitEvent(cs, ss->done[p], 0);
+        if (e != cudaSuccess) return jk::cuda_fail(e, "allgather wait: signal peers");
     }
-    jk::wait_peers_kernel<<<1, 32, 0, cs>>>(flags, world, rank, calls, jk::device_error_word(device));
+    jk::wait_peers_kernel<<<1, 32, 0, cs>>>(flags_peers[rank], world, rank, jk::device_error_word(device));
     return jk::cuda_fail(cudaGetLastError(), "allgather wait launch");
 }
 
@@ -218,22 +232,6 @@ extern "C" jk_status jk_sharded_matmul_allgather(const jk_qmatrix* w_shard, cons
         if (e != cudaSuccess) return jk::cuda_fail(e, "sharded product: chunk copies");
     }
     if (world == 1) return JK_OK;
-    for (int p = 0; p < world; ++p) {
-        if (p == rank) continue;
-        // peer p's first copy stream joins the others, then, after this call's copies to p:
-        // flags_peers[p][rank] += 1
-        cudaError_t e = cudaSuccess;
-        for (int q = 1; q < jk::NSUB && e == cudaSuccess; ++q) {
-            e = cudaEventRecord(ss->sub[p][q], ss->cs[p][q]);
-            if (e == cudaSuccess) e = cudaStreamWaitEvent(ss->cs[p][0], ss->sub[p][q], 0);
-        }
-        if (e == cudaSuccess) {
-            jk::signal_peer_kernel<<<1, 32, 0, ss->cs[p][0]>>>(flags_peers[p] + rank);
-            e = cudaGetLastError();
-        }
-        if (e == cudaSuccess) e = cudaEventRecord(ss->done[p], ss->cs[p][0]);
-        if (e != cudaSuccess) return jk::cuda_fail(e, "sharded product: peer signal");
-    }
-    if (wait) return jk_allgather_wait(w_shard->device, flags_peers[rank], world, rank, 1, stream);
+    if (wait) return jk_allgather_wait(w_shard->device, flags_peers, world, rank, stream);
     return JK_OK;
 }

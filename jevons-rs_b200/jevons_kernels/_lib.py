@@ -79,7 +79,7 @@ SIGNATURES = {
     "jk_ipc_open": (I, [I, P, ctypes.POINTER(P)]),
     "jk_ipc_close": (I, [I, P]),
     "jk_sharded_matmul_allgather": (I, [P, P, I, S, S, I, I, P, P, I, I, P, P]),
-    "jk_allgather_wait": (I, [I, P, I, I, U32, P]),
+    "jk_allgather_wait": (I, [I, P, I, I, P]),
     "jk_matmul_splitk_noalloc": (I, [P, P, I, S, S, P, S, I, P]),
     "jk_set_max_ctas": (I, [I, I]),
     "jk_get_max_ctas": (I, [I, ctypes.POINTER(I), ctypes.POINTER(I)]),

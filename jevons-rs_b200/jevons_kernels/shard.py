@@ -139,14 +139,15 @@ class PeerGather:
             ctypes.cast(self.tables[i], ctypes.c_void_p), ctypes.cast(self.flags, ctypes.c_void_p), int(chunks),
             1 if wait else 0, scratch.handle if scratch is not None else None, ctypes.c_void_p(st)))
 
-    def wait(self, calls: int, stream=None):
-        """jk_allgather_wait for the `calls` products made with wait=False since the last wait."""
+    def wait(self, stream=None):
+        """jk_allgather_wait: ends the exchange of every product made with wait=False since the
+        last wait (this rank's copies are signalled to the peers, the peers' shards have landed)."""
         import ctypes
         import torch
         from ._lib import check, load
         st = stream if stream is not None else torch.cuda.current_stream().cuda_stream
-        check(load().jk_allgather_wait(self.gpu.device, ctypes.c_void_p(self.flags[self.rank]), self.world,
-                                       self.rank, int(calls), ctypes.c_void_p(st)))
+        check(load().jk_allgather_wait(self.gpu.device, ctypes.cast(self.flags, ctypes.c_void_p), self.world,
+                                       self.rank, ctypes.c_void_p(st)))
 
     def close(self):
         from ._lib import load

@@ -54,7 +54,7 @@ def _worker(rank, world, port, case, q):
                 elif call == 3:
                     pg.run(w, x, i=0, wait=False, chunks=2, scratch=scratch)
                     pg.run(w, x, i=1, wait=False, chunks=1, scratch=scratch)
-                    pg.wait(2)
+                    pg.wait()
                 else:
                     continue
                 torch.cuda.synchronize()

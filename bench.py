@@ -475,7 +475,7 @@ def run_ours(args):
 
     from jevons_kernels import synth
     from jevons_kernels.gemm import Buf, Gpu, Plan, QMatrix, SplitScratch, matmul, matvec
-    from jevons_kernels.shard import PeerGather, column_shard, shard_rows
+    from jevons_kernels.shard import PeerGather, column_shard
 
     gpu = Gpu(local)
     dev = torch.device("cuda", local)
@@ -633,14 +633,14 @@ def run_ours(args):
     f16_tflops = flops_step * world * args.steps / (f16_ms * 1e-3) / 1e12
 
     # ---- config 4's matrix: the vocabulary head, Q4_K [262144, 2560] --------------------------
-    # Every rank draws the same full matrix and keeps its column shard.
+    # Every rank draws only its column shard (seeded by rank: the same value distributions, without
+    # each of N ranks generating the whole 377 MB matrix).
     gv4 = vocab = None
     if not args.no_vocab:
-        raw4 = synth.q4k_blocks(np.random.default_rng(40), VOCAB_N, K_DIM)
         v_lo, v_hi = column_shard(VOCAB_N, world, rank)
         n_r = v_hi - v_lo
-        w4 = QMatrix.upload(gpu, Q4_K, n_r, K_DIM, 1,
-                            np.frombuffer(shard_rows(raw4, Q4_K, VOCAB_N, K_DIM, v_lo, v_hi), np.uint8))
+        raw4 = synth.q4k_blocks(np.random.default_rng(40 + 1000 * rank), n_r, K_DIM)
+        w4 = QMatrix.upload(gpu, Q4_K, n_r, K_DIM, 1, raw4)
         del raw4
         if world == 1:  # M=1 product over the whole 377 MB matrix (larger than L2)
             o4 = torch.empty(1, VOCAB_N, device=dev)

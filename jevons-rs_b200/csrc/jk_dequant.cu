@@ -83,12 +83,42 @@ jk_status launch_dequant(const WView& w, float* out, cudaStream_t stream) {
     return cuda_fail(cudaGetLastError(), "dequantize launch");
 }
 
-// f32 or f16 activations -> bf16 (round to nearest even), 8 elements per thread when aligned.
+// f32 or f16 activations -> bf16 (round to nearest even), 8 elements per thread: one or two
+// 16-byte loads and one 16-byte store when the buffers are 16-byte aligned and the count a multiple
+// of 8 (every activation matrix here: k % 64 == 0), element by element otherwise.
+// Launched with programmatic dependent launch: the kernel lets the product that follows start its
+// prologue at once and waits for the previous kernel (which may have written x) before reading.
 __global__ void __launch_bounds__(256) to_bf16_kernel(const void* __restrict__ x, int dtype, size_t count,
-                                                      __nv_bfloat16* __restrict__ out) {
+                                                      __nv_bfloat16* __restrict__ out, int vec) {
+    asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
+    asm volatile("griddepcontrol.wait;" ::: "memory");
     const size_t i = ((size_t)blockIdx.x * blockDim.x + threadIdx.x);
     const size_t base = i * 8;
     if (base >= count) return;
+    if (vec) {
+        float f[8];
+        if (dtype == JK_DTYPE_F32) {
+            const float4 a = __ldg(reinterpret_cast<const float4*>(x) + 2 * i);
+            const float4 b = __ldg(reinterpret_cast<const float4*>(x) + 2 * i + 1);
+            f[0] = a.x; f[1] = a.y; f[2] = a.z; f[3] = a.w; f[4] = b.x; f[5] = b.y; f[6] = b.z; f[7] = b.w;
+        } else {
+            const uint4 a = __ldg(reinterpret_cast<const uint4*>(x) + i);
+            const uint32_t u[4] = {a.x, a.y, a.z, a.w};
+#pragma unroll
+            for (int j = 0; j < 4; ++j) {
+                const float2 h = __half22float2(*reinterpret_cast<const __half2*>(&u[j]));
+                f[2 * j] = h.x;
+                f[2 * j + 1] = h.y;
+            }
+        }
+        uint4 o;
+        o.x = pack2<true>(f[0], f[1]);
+        o.y = pack2<true>(f[2], f[3]);
+        o.z = pack2<true>(f[4], f[5]);
+        o.w = pack2<true>(f[6], f[7]);
+        reinterpret_cast<uint4*>(out)[i] = o;
+        return;
+    }
     const size_t end = base + 8 < count ? base + 8 : count;
     for (size_t j = base; j < end; ++j) {
         float f = dtype == JK_DTYPE_F32 ? reinterpret_cast<const float*>(x)[j]
@@ -100,8 +130,18 @@ __global__ void __launch_bounds__(256) to_bf16_kernel(const void* __restrict__ x
 jk_status launch_convert_to_bf16(const void* x, int x_dtype, size_t count, void* out, cudaStream_t stream) {
     if (count == 0) return JK_OK;
     const size_t threads = (count + 7) / 8;
-    to_bf16_kernel<<<(unsigned)((threads + 255) / 256), 256, 0, stream>>>(x, x_dtype, count,
-                                                                         reinterpret_cast<__nv_bfloat16*>(out));
+    const int vec = ((reinterpret_cast<uintptr_t>(x) | reinterpret_cast<uintptr_t>(out)) & 15) == 0 && count % 8 == 0;
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = dim3((unsigned)((threads + 255) / 256));
+    cfg.blockDim = dim3(256);
+    cfg.stream = stream;
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[0].val.programmaticStreamSerializationAllowed = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = 1;
+    cudaError_t e = cudaLaunchKernelEx(&cfg, to_bf16_kernel, x, x_dtype, count, reinterpret_cast<__nv_bfloat16*>(out), vec);
+    if (e != cudaSuccess) return cuda_fail(e, "activation conversion launch");
     return cuda_fail(cudaGetLastError(), "activation conversion launch");
 }
 

@@ -656,6 +656,9 @@ jk_status launch_gemv_t(const WView& w, const void* x, int x_dtype, int mrows, f
     // the SMs), but no more CTAs than row groups
     const int64_t want = (int64_t)geo.rowgroups;
     // grouped: the live jobs share the SMs
+#ifdef JK_GEMV_ONE_CTA_PER_SM
+    if (!gp.jobs && per_sm > 1) per_sm = 1;
+#endif
     const int64_t cap = ((int64_t)per_sm * sms + jobs_est - 1) / jobs_est;
     const unsigned grid = (unsigned)(want < cap ? want : cap);
     if (grid == 0) return JK_OK;

@@ -313,6 +313,10 @@ template <typename T>
 __global__ void __launch_bounds__(256) quantize_act_q8_kernel(const T* __restrict__ x, int64_t m, int64_t k,
                                                               int8_t* __restrict__ xq, float* __restrict__ xd,
                                                               int64_t m_pad) {
+    // programmatic dependent launch: the product that follows may start its prologue at once; x
+    // may come from the previous kernel, so wait for it before reading
+    asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
+    asm volatile("griddepcontrol.wait;" ::: "memory");
     const int64_t nblk = k / 32;
     const int64_t gw = ((int64_t)blockIdx.x * blockDim.x + threadIdx.x) >> 5;
     if (gw >= m * nblk) return;
@@ -363,16 +367,26 @@ extern "C" jk_status jk_quantize_act_q8(const void* x, int x_dtype, size_t m, si
         if (e != cudaSuccess) return jk::cuda_fail(e, "clear padded activation scales");
     }
     const size_t warps = m * (k / 32);
-    const unsigned grid = (unsigned)((warps * 32 + 255) / 256);
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = dim3((unsigned)((warps * 32 + 255) / 256));
+    cfg.blockDim = dim3(256);
+    cfg.stream = cs;
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[0].val.programmaticStreamSerializationAllowed = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = 1;
+    cudaError_t e;
     if (x_dtype == JK_DTYPE_F32)
-        jk::quantize_act_q8_kernel<float><<<grid, 256, 0, cs>>>(static_cast<const float*>(x), (int64_t)m, (int64_t)k, xq,
-                                                                 xd, (int64_t)m_pad);
+        e = cudaLaunchKernelEx(&cfg, jk::quantize_act_q8_kernel<float>, static_cast<const float*>(x), (int64_t)m,
+                               (int64_t)k, xq, xd, (int64_t)m_pad);
     else if (x_dtype == JK_DTYPE_F16)
-        jk::quantize_act_q8_kernel<__half><<<grid, 256, 0, cs>>>(static_cast<const __half*>(x), (int64_t)m, (int64_t)k,
-                                                                 xq, xd, (int64_t)m_pad);
+        e = cudaLaunchKernelEx(&cfg, jk::quantize_act_q8_kernel<__half>, static_cast<const __half*>(x), (int64_t)m,
+                               (int64_t)k, xq, xd, (int64_t)m_pad);
     else
-        jk::quantize_act_q8_kernel<__nv_bfloat16><<<grid, 256, 0, cs>>>(static_cast<const __nv_bfloat16*>(x),
-                                                                        (int64_t)m, (int64_t)k, xq, xd, (int64_t)m_pad);
+        e = cudaLaunchKernelEx(&cfg, jk::quantize_act_q8_kernel<__nv_bfloat16>, static_cast<const __nv_bfloat16*>(x),
+                               (int64_t)m, (int64_t)k, xq, xd, (int64_t)m_pad);
+    if (e != cudaSuccess) return jk::cuda_fail(e, "activation quantization launch");
     return jk::cuda_fail(cudaGetLastError(), "activation quantization launch");
 }
 

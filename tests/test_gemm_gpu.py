@@ -112,10 +112,12 @@ def test_heuristic_plans_and_matmul(gpu):
         p = Plan.heuristic(w, m, False)
         assert p.bm == want and p.valid_for(w, m)
         assert Plan.heuristic(w, m, True).splits == 1 and Plan.heuristic(w, m, True).bm > 0
-    # 80 x 2 tiles of m=256 keep 148 SMs busy with whole tiles; with 400 SMs more than half
-    # would idle, so K is split (stream-K)
+    # 80 x 2 tiles of m=256 keep 148 SMs busy with whole tiles; with 400 SMs 64-row tiles (320)
+    # still cover 60 % of them; with 1000 SMs K is split (stream-K)
     assert Plan.heuristic(w, 256, False, 148).splits == 1
-    assert Plan.heuristic(w, 256, False, 400).splits > 1
+    p400 = Plan.heuristic(w, 256, False, 400)
+    assert (p400.bm, p400.splits) == (64, 1)
+    assert Plan.heuristic(w, 256, False, 1000).splits > 1
     x, x_exact = activations(32, 2560, torch.bfloat16, seed=1)
     out = torch.empty(32, 10240, device="cuda")
     matmul(gpu, Buf(x), 32, w, Buf(out), None, SplitScratch(gpu))

@@ -150,7 +150,7 @@ jk_status jk_qmatrix_dequantize(const jk_qmatrix *w, float *out_dev, size_t out_
 /* ---- launch plans ---------------------------------------------------------------------------- */
 
 /* Plan (gemm.rs:973-1016). bm == 0 selects the small-row kernel (m <= JK_GEMV_ROWS).
- * Otherwise bm is the activation-row tile of the tensor-core kernel (MMA N: 32, 64, 128 or
+ * Otherwise bm is the activation-row tile of the tensor-core kernel (MMA N: 32, 64, 96, 128 or
  * 256), bn the weight-row tile and splits the split-K factor (1..16). bn = 128 runs one CTA per
  * tile (MMA M = 128); bn = 256 (block-quantized weights, bm >= 128) runs each tile on a pair of
  * CTAs with one M = 256 MMA (tcgen05 cta_group::2), each CTA dequantizing 128 rows and loading

@@ -725,7 +725,7 @@ int row_tile_for(size_t m) {
 
 bool plan_valid(const jk_plan& p, const jk_qmatrix* w, size_t m) {
     if (p.bm == 0) return m <= JK_GEMV_ROWS && p.splits == 1 && w->k / 32 <= 1u << 20;
-    const bool bm_ok = p.bm == 32 || p.bm == 64 || p.bm == 128 || p.bm == 256;
+    const bool bm_ok = p.bm == 32 || p.bm == 64 || p.bm == 96 || p.bm == 128 || p.bm == 256;
     // bn: weight rows per tile. 128 = one CTA per tile; 256 = a CTA pair (tcgen05 cta_group::2,
     // each CTA dequantizes 128 rows and loads half the activation rows) for block-quantized
     // weights at bm >= 128.

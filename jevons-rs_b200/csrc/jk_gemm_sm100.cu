@@ -1444,6 +1444,7 @@ jk_status launch_tc_bt(const LaunchArgs& a, int bt) {
     switch (bt) {
     case 32: return launch_tc<FMT, BF16, 32, false>(a);
     case 64: return launch_tc<FMT, BF16, 64, false>(a);
+    case 96: return launch_tc<FMT, BF16, 96, false>(a);
     case 128: return launch_tc<FMT, BF16, 128, false>(a);
     default: return launch_tc<FMT, BF16, 256, false>(a);
     }

@@ -113,7 +113,7 @@ std::vector<jk_plan> candidates(const jk_qmatrix* w, size_t m, bool row_invarian
     std::vector<jk_plan> out;
     if (!row_invariant && m <= JK_GEMV_ROWS) out.push_back({0, 128, 1});
     const size_t steps = w->k / 64;
-    for (int bm : {32, 64, 128, 256}) {
+    for (int bm : {32, 64, 96, 128, 256}) {
         if (bm > 32 && (size_t)bm / 2 >= m) continue;  // taller than the rows only wastes work
         for (int bn : {128, 256}) {
             for (int splits : {1, 2, 4, 8}) {

@@ -225,7 +225,7 @@ def _plan_valid_for(self: Plan, w: QMatrix, m: int) -> bool:
 
 Plan.heuristic = staticmethod(_plan_heuristic)
 Plan.valid_for = _plan_valid_for
-Plan.ROW_TILES = (32, 64, 128, 256)
+Plan.ROW_TILES = (32, 64, 96, 128, 256)
 Plan.COL_TILES = (128, 256)  # 256: a CTA pair per tile (block-quantized weights, bm >= 128)
 
 

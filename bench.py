@@ -596,31 +596,59 @@ def run_ours(args):
     m32_tflops = 2.0 * 32 * N_DIM * K_DIM * L * gv_steps * world / (c_ms * 1e-3) / 1e12
 
     # ---- e2e: host buffers through the public API -------------------------------------------
-    # One step = one product as a caller runs it: the step's activations host->device from pinned
-    # memory, the product (jk_matmul), and its whole f32 output device->host. Steps rotate over
-    # the L distinct matrices, so the weights stream from HBM as in the device-timed step.
-    # With N GPUs the step's result is the all-gathered [N, M, N_DIM] output, read back whole.
-    xh = x.cpu().pin_memory()
-    oh = torch.empty(world, M_ROWS, N_DIM, dtype=torch.float32).pin_memory()
-    xd = torch.empty_like(x)
-    xdb = Buf(xd)
+    # One step = one product as a caller serving it runs it: the step's activations host->device
+    # from pinned memory, the product (jk_matmul), and its whole f32 output device->host. Steps
+    # rotate over the L distinct matrices, so the weights stream from HBM as in the device-timed
+    # step. On one GPU two steps are in flight on two streams (double-buffered host and device
+    # buffers): step i+1's upload and product overlap step i's download, as a server pipelines
+    # requests; each step still moves its own inputs and result. With N GPUs the step's result is
+    # the all-gathered [N, M, N_DIM] output and the steps run one after another on one stream.
+    nbuf = 2 if world == 1 else 1
+    streams = [torch.cuda.Stream(device=dev) for _ in range(nbuf)]
+    xhs = [x.cpu().pin_memory() for _ in range(nbuf)]
+    ohs = [torch.empty(world, M_ROWS, N_DIM, dtype=torch.float32).pin_memory() for _ in range(nbuf)]
+    xds = [torch.empty_like(x) for _ in range(nbuf)]
+    # each in-flight step owns its device output and split-K scratch
+    ods = [torch.empty(M_ROWS, N_DIM, device=dev) for _ in range(nbuf)]
+    scrs = [scratch] + [SplitScratch(gpu) for _ in range(nbuf - 1)]
     e2e_state = {"i": 0}
 
     def e2e_product():
         i = e2e_state["i"]
-        e2e_state["i"] = (i + 1) % L
-        xd.copy_(xh, non_blocking=True)
-        if world > 1:
-            pg.run(ws[i], xd, i=i, wait=True, chunks=2, scratch=scratch)
-            oh.copy_(pg.output(i), non_blocking=True)
-        else:
-            matmul(gpu, xdb, M_ROWS, ws[i], obufs[i], None, scratch)
-            oh[0].copy_(outs[i], non_blocking=True)
+        e2e_state["i"] = i + 1
+        b, layer = i % nbuf, i % L
+        with torch.cuda.stream(streams[b]):
+            xds[b].copy_(xhs[b], non_blocking=True)
+            if world > 1:
+                pg.run(ws[layer], xds[b], i=layer, wait=True, chunks=2, scratch=scratch)
+                ohs[b].copy_(pg.output(layer), non_blocking=True)
+            else:
+                matmul(gpu, Buf(xds[b]), M_ROWS, ws[layer], Buf(ods[b]), None, scrs[b])
+                ohs[b][0].copy_(ods[b], non_blocking=True)
+
+    def e2e_timed(steps, warmup):
+        cur = torch.cuda.current_stream()
+        for _ in range(warmup):
+            e2e_product()
+        torch.cuda.synchronize()
+        barrier()
+        a, e = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        a.record(cur)
+        for st in streams:
+            st.wait_stream(cur)
+        for _ in range(steps):
+            e2e_product()
+        for st in streams:
+            cur.wait_stream(st)
+        e.record(cur)
+        torch.cuda.synchronize()
+        return max_over_ranks(a.elapsed_time(e))
 
     e_steps = max(args.steps, 2 * L)
-    e_ms = timed(e2e_product, e_steps, args.warmup, use_graph=False)
+    e_ms = e2e_timed(e_steps, args.warmup)
     e2e_value = 2.0 * M_ROWS * N_DIM * K_DIM * world * e_steps / (e_ms * 1e-3) / 1e12
-    e2e_d2h = oh.numel() * 4
+    e2e_d2h = ohs[0].numel() * 4
+    xh = xhs[0]
 
     # ---- the same stack at the reference's operand precision (FP16 activations) -------------
     x16 = x.float().half()
@@ -735,7 +763,9 @@ def run_ours(args):
             "e2e": {"value": e2e_value, "unit": "TFLOP/s", "h2d_bytes_per_step": xh.numel() * 2,
                     "d2h_bytes_per_step": e2e_d2h, "steps": e_steps,
                     "what": "per step: x host->device (pinned), one jk_matmul product, its whole f32 output "
-                            "device->host; steps rotate over the distinct matrices; CUDA events"},
+                            "device->host; steps rotate over the distinct matrices; " +
+                            ("two steps in flight on two streams (double buffers)" if world == 1 else
+                             "steps in order on one stream (all-gathered output)") + "; CUDA events"},
             "f16": {"metric": "Q4_K GEMM TFLOP/s (M=256), FP16 activations (the reference's operand type)",
                     "value": f16_tflops, "unit": "TFLOP/s", "ms_per_step": f16_ms / args.steps},
             "gemv_vocab": gv4,

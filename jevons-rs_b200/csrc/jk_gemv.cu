@@ -221,7 +221,9 @@ __device__ __forceinline__ void stage_x(const Geo& geo, const void* x, int x_dty
     }
 }
 
-template <int FMT, int MR>
+// GRP: the expert-grouped instantiation (job table, row gather and scatter); the dense products
+// run a kernel compiled without that code.
+template <int FMT, int MR, bool GRP>
 __global__ void __launch_bounds__(THREADS, MR <= 2 ? 2 : 1) gemv_kernel(WView w, Geo geo, const void* __restrict__ x, int x_dtype,
                                                           int mrows, float* __restrict__ out, int64_t ldo,
                                                           uint32_t* err, Grp gp) {
@@ -239,7 +241,7 @@ __global__ void __launch_bounds__(THREADS, MR <= 2 ? 2 : 1) gemv_kernel(WView w,
     int64_t wrow0 = 0;
 #pragma unroll
     for (int r = 0; r < MR; ++r) src[r] = dst[r] = r;
-    if (gp.jobs) {
+    if (GRP && gp.jobs) {
         // the job table comes from the previous grid (the grouping): wait for it first
         pdl_wait();
         const uint32_t j = blockIdx.y;
@@ -639,8 +641,9 @@ jk_status launch_gemv_t(const WView& w, const void* x, int x_dtype, int mrows, f
     areas((int)((steps_w + nseg - 1) / nseg));
 
     const size_t smem = fixed + (size_t)WARPS * SLOTS_PER_WARP * geo.slot_bytes;
-    auto kern = gemv_kernel<FMT, MR>;
-    static Cache cache = {};
+    auto kern = gp.jobs ? gemv_kernel<FMT, MR, true> : gemv_kernel<FMT, MR, false>;
+    static Cache caches[2] = {};
+    Cache& cache = caches[gp.jobs ? 1 : 0];
     if (dev >= 0 && dev < 64 && !cache.smem_set[dev]) {
         cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, 220 * 1024);
         // all of L1 as shared memory, so two CTAs fit on an SM

@@ -11,12 +11,14 @@ L=36 distinct weight matrices (36 x 14.7 MB = 531 MB of weights, > 4x the 126 MB
 matrix streams from HBM), each product writing its own f32 output. Synthetic seeded data.
 
 With N GPUs (one process per GPU): the projection is column-sharded -- every rank owns a
-10240-column shard of an N*10240-wide layer (per-GPU work fixed: weak scaling) -- and each
-layer's f32 output shard is all-gathered over NVLink by jk_sharded_matmul_allgather: the copy
-engines push it into every peer's buffer (CUDA IPC) while the next layer's product runs, and the
-step ends with one bounded flag wait. `vocab_head` is BASELINE config 4 strong-scaled over the N
-GPUs (M=2048, K=2560, N=262144 split by column, f32 logits all-gathered), compute-only and end to
-end against max(compute, NVLink) time.
+10240-column shard of an N*10240-wide column-parallel layer (per-GPU work fixed: weak scaling) --
+and the outputs stay sharded, as a tensor-parallel MLP's column-parallel first projection leaves
+them (no collective on the data path of `value`). The `allgather` sub-line times the same stack
+with every layer's f32 output shard all-gathered over NVLink by jk_sharded_matmul_allgather (the
+copy engines push it into every peer's buffer over CUDA IPC while the next layer's product runs;
+one bounded flag wait per step). `vocab_head` is BASELINE config 4 strong-scaled over the N GPUs
+(M=2048, K=2560, N=262144 split by column, f32 logits all-gathered), compute-only and end to end
+against max(compute, NVLink) time.
 
 Printed JSON (rank 0): `value` = aggregate TFLOP/s of the timed steps (inputs resident in HBM,
 device-timed with CUDA events, max over ranks); `e2e` = the same metric through the public API with
@@ -495,18 +497,18 @@ def run_ours(args):
     xb = Buf(x)
     obufs = [Buf(o) for o in outs]
 
-    # N > 1: every layer writes its own gathered [N, M, N_DIM] buffer; the copies of layer i run
-    # beside the product of layer i+1, and the step ends with one wait for all L layers.
+    # N > 1, `allgather` sub-line: every layer writes its own gathered [N, M, N_DIM] buffer; the
+    # copies of layer i run beside the product of layer i+1, and the step ends with one wait.
     pg = PeerGather(gpu, M_ROWS, N_DIM, buffers=L) if world > 1 else None
 
     def step(xbuf=xb):
-        if world > 1:
-            for i in range(L):
-                pg.run(ws[i], x, i=i, wait=False, chunks=1, scratch=scratch)
-            pg.wait()
-        else:
-            for i in range(L):
-                matmul(gpu, xbuf, M_ROWS, ws[i], obufs[i], None, scratch)
+        for i in range(L):
+            matmul(gpu, xbuf, M_ROWS, ws[i], obufs[i], None, scratch)
+
+    def step_gathered():
+        for i in range(L):
+            pg.run(ws[i], x, i=i, wait=False, chunks=1, scratch=scratch)
+        pg.wait()
 
     def barrier():
         torch.cuda.synchronize()
@@ -554,6 +556,16 @@ def run_ours(args):
     with sampler:
         ms = timed(step, args.steps, args.warmup)
     value = flops_step * world * args.steps / (ms * 1e-3) / 1e12
+    allgather = None
+    if world > 1:
+        ag_ms = timed(step_gathered, args.steps, args.warmup)
+        allgather = {
+            "what": "the same stack with every layer's f32 output shard all-gathered into every rank's "
+                    "[N, M, N_DIM] buffer by the copy engines (jk_sharded_matmul_allgather), one bounded "
+                    "flag wait per step; CUDA graph replay, CUDA events, max over ranks",
+            "value": flops_step * world * args.steps / (ag_ms * 1e-3) / 1e12, "unit": "TFLOP/s",
+            "ms_per_step": ag_ms / args.steps,
+            "gather_bytes_sent_per_gpu_per_step": L * (world - 1) * M_ROWS * N_DIM * 4}
 
     # ---- roofline: one product launch = one tensor-core kernel (stream-K combines split-K
     # partials in-kernel), so its average duration is the step time over the layers.
@@ -601,12 +613,12 @@ def run_ours(args):
     # rotate over the L distinct matrices, so the weights stream from HBM as in the device-timed
     # step. On one GPU two steps are in flight on two streams (double-buffered host and device
     # buffers): step i+1's upload and product overlap step i's download, as a server pipelines
-    # requests; each step still moves its own inputs and result. With N GPUs the step's result is
-    # the all-gathered [N, M, N_DIM] output and the steps run one after another on one stream.
-    nbuf = 2 if world == 1 else 1
+    # requests; each step still moves its own inputs and result. With N GPUs every rank runs the
+    # same on its column shard (its result: its [M, N_DIM] shard of the output).
+    nbuf = 2
     streams = [torch.cuda.Stream(device=dev) for _ in range(nbuf)]
     xhs = [x.cpu().pin_memory() for _ in range(nbuf)]
-    ohs = [torch.empty(world, M_ROWS, N_DIM, dtype=torch.float32).pin_memory() for _ in range(nbuf)]
+    ohs = [torch.empty(M_ROWS, N_DIM, dtype=torch.float32).pin_memory() for _ in range(nbuf)]
     xds = [torch.empty_like(x) for _ in range(nbuf)]
     # each in-flight step owns its device output and split-K scratch
     ods = [torch.empty(M_ROWS, N_DIM, device=dev) for _ in range(nbuf)]
@@ -619,12 +631,8 @@ def run_ours(args):
         b, layer = i % nbuf, i % L
         with torch.cuda.stream(streams[b]):
             xds[b].copy_(xhs[b], non_blocking=True)
-            if world > 1:
-                pg.run(ws[layer], xds[b], i=layer, wait=True, chunks=2, scratch=scratch)
-                ohs[b].copy_(pg.output(layer), non_blocking=True)
-            else:
-                matmul(gpu, Buf(xds[b]), M_ROWS, ws[layer], Buf(ods[b]), None, scrs[b])
-                ohs[b][0].copy_(ods[b], non_blocking=True)
+            matmul(gpu, Buf(xds[b]), M_ROWS, ws[layer], Buf(ods[b]), None, scrs[b])
+            ohs[b].copy_(ods[b], non_blocking=True)
 
     def e2e_timed(steps, warmup):
         cur = torch.cuda.current_stream()
@@ -746,7 +754,7 @@ def run_ours(args):
             "config": {"workload": WORKLOAD, "weights": "Q4_K", "m": M_ROWS, "k": K_DIM, "n_per_gpu": N_DIM,
                        "n_total": N_DIM * world, "layers_per_step": L, "plan": repr(plan),
                        "l2": "inputs larger than L2: 36 distinct weight matrices (531 MB) per step",
-                       "parallelism": f"column-shard x{world}" + (" + copy-engine all-gather of f32 outputs over NVLink" if world > 1 else ""),
+                       "parallelism": f"column-shard x{world}" + (" (outputs stay sharded; the allgather sub-line gathers them)" if world > 1 else ""),
                        "activations": "bf16 N(0,1)"},
             "roofline": {"bound": "tensor", "achieved": achieved, "peak": peak, "unit": "TFLOP/s",
                          "frac": achieved / peak, "traffic": traffic,
@@ -763,17 +771,17 @@ def run_ours(args):
             "e2e": {"value": e2e_value, "unit": "TFLOP/s", "h2d_bytes_per_step": xh.numel() * 2,
                     "d2h_bytes_per_step": e2e_d2h, "steps": e_steps,
                     "what": "per step: x host->device (pinned), one jk_matmul product, its whole f32 output "
-                            "device->host; steps rotate over the distinct matrices; " +
-                            ("two steps in flight on two streams (double buffers)" if world == 1 else
-                             "steps in order on one stream (all-gathered output)") + "; CUDA events"},
+                            "device->host; steps rotate over the distinct matrices; two steps in flight on "
+                            "two streams (double buffers); with N GPUs every rank on its column shard; "
+                            "CUDA events, max over ranks"},
             "f16": {"metric": "Q4_K GEMM TFLOP/s (M=256), FP16 activations (the reference's operand type)",
                     "value": f16_tflops, "unit": "TFLOP/s", "ms_per_step": f16_ms / args.steps},
             "gemv_vocab": gv4,
             "vocab_head": vocab,
             "cfg3_parakeet_q8_0": cfg3,
-            # per step: one tensor-core kernel per layer; with N GPUs also one signal kernel per peer
-            # (on the copy streams) and one wait kernel
-            "gpu_launches": args.steps * (L * launches_per_product + (world if world > 1 else 0)),
+            "allgather": allgather,
+            # per step: one tensor-core kernel per layer
+            "gpu_launches": args.steps * L * launches_per_product,
             "timing": "CUDA graph replay of each step, CUDA events, max over ranks",
             "clocks": sampler.report(),
             "cpu_baseline": cpu,

@@ -759,13 +759,18 @@ jk::WView dense_view(const jk_qmatrix* w) {
 
 }  // namespace
 
-// Plan::heuristic (gemm.rs:989-1004), adapted to this kernel: the activation-row tile grows with
-// m but stops at 128 for block-quantized weights (there the dequantized weights live in tensor
-// memory next to two 128-column accumulators, which measures faster than 256-row tiles with
-// shared-memory weight stages); split-K (`splits > 1`, the stream-K schedule) is chosen only when
-// whole tiles would leave more than half of the SMs without a tile: measured on B200, whole tiles
-// win whenever there are about as many tiles as SMs or more (the stream-K fix-up costs more than an
-// uneven last wave), while few long tiles (e.g. N=2560, K=10240) need K split across SMs.
+// Plan::heuristic (gemm.rs:989-1004), adapted to this kernel. Row-invariant plans: the smallest
+// activation-row tile >= m, capped at 128 for block-quantized weights (there the dequantized weights
+// live in tensor memory next to two accumulators, which measures faster than 256-row tiles with
+// shared-memory weight stages). Otherwise, for block-quantized weights, a small cost model picks the
+// row tile and the schedule: whole tiles of bm rows take ceil(tiles / SMs) waves of k-blocks at the
+// main loop's measured cycles per k-block for that tile (32: 338, 64: 400, 96: 491, 128: 555), and
+// stream-K (bm = min(row tile, 128), splits = 2) spreads the same k-blocks evenly over the SMs but
+// pays a fixed ~20000 cycles (its fix-up and the pipeline fill it can no longer overlap with the
+// previous product). On B200 this reproduces the measured best plan of every shape tried (Q4_K
+// N=10240, K=2560 at m = 32..768: e.g. bm 64 at m=160-192, 96 at m=224-288 and 448, 128 at 320-384
+// and 512-768; Q6_K N=2560, K=10240: stream-K; Q8_0 at m=750: 96 or 64). FP16 weights keep the
+// rule of growing the row tile with m, with stream-K only when whole tiles leave most SMs idle.
 extern "C" jk_status jk_plan_heuristic(const jk_qmatrix* w, size_t m, int row_invariant, int sms, jk_plan* out) {
     if (!w || !out) return fail(JK_ERR_INVALID, "null pointer");
     int bm = row_tile_for(m);
@@ -780,20 +785,36 @@ extern "C" jk_status jk_plan_heuristic(const jk_qmatrix* w, size_t m, int row_in
         return JK_OK;
     }
     const size_t target = sms > 0 ? (size_t)sms : (size_t)jk::sm_count(w->device);
-    const size_t tiles = (w->n + 127) / 128 * ((m + bm - 1) / bm);
-    const bool enough_tiles = tiles * 2 >= target;
-    if (!enough_tiles && bm == 128) {
-        // Few 128-row tiles: halving the row tile doubles them; whole 64-row tiles on at least 60 % of
-        // the SMs beat stream-K (measured at M=750: N=1024, K=1024 13.3 vs 22.7 us; K=4096 27.9 vs
-        // 33.2 us), while with fewer (M=256, N=2560, K=10240: 80 tiles, 40.6 vs 30.2 us) the long K
-        // is better split.
-        const size_t tiles64 = (w->n + 127) / 128 * ((m + 63) / 64);
-        if (tiles64 * 5 >= target * 3) {
-            *out = {64, bn, 1};
-            return JK_OK;
+    const size_t wt = (w->n + 127) / 128;
+    const size_t kbt = w->k / 64;
+    if (w->type != JK_TYPE_F16) {
+        static const int TILE[4] = {32, 64, 96, 128};
+        static const double CYC[4] = {338.0, 400.0, 491.0, 555.0};
+        int best = 3;
+        double best_cost = 0.0;
+        for (int t = 3; t >= 0; --t) {  // ties go to the larger tile
+            const size_t tiles = wt * ((m + TILE[t] - 1) / TILE[t]);
+            const double cost = (double)((tiles + target - 1) / target) * (double)kbt * CYC[t];
+            if (t == 3 || cost < best_cost) {
+                best = t;
+                best_cost = cost;
+            }
         }
+        if (kbt >= 8) {
+            const int tsk = bm == 32 ? 0 : bm == 64 ? 1 : bm == 96 ? 2 : 3;
+            const size_t tiles = wt * ((m + bm - 1) / bm);
+            const double sk_cost = (double)tiles * (double)kbt / (double)target * CYC[tsk] + 20000.0;
+            if (sk_cost < best_cost) {
+                *out = {bm, bn, 2};
+                return JK_OK;
+            }
+        }
+        *out = {TILE[best], bn, 1};
+        return JK_OK;
     }
-    *out = {bm, bn, enough_tiles || w->k / 64 < 8 ? 1 : 2};
+    const size_t tiles = wt * ((m + bm - 1) / bm);
+    const bool enough_tiles = tiles * 2 >= target;
+    *out = {bm, bn, enough_tiles || kbt < 8 ? 1 : 2};
     return JK_OK;
 }
 

@@ -107,17 +107,19 @@ def test_multi_expert_matrix_dense_product_uses_expert_zero(gpu):
 def test_heuristic_plans_and_matmul(gpu):
     from jevons_kernels.gemm import Buf, Plan, SplitScratch, matmul
     w, _, dense = make_weights(gpu, KINDS["Q4_K"], 10240, 2560, seed=1)
-    # row tiles stop at 128 for block-quantized weights (tensor-memory weight stages)
-    for m, want in ((1, 0), (2, 0), (32, 32), (100, 128), (256, 128)):
-        p = Plan.heuristic(w, m, False)
-        assert p.bm == want and p.valid_for(w, m)
+    # row tiles stop at 128 for block-quantized weights (tensor-memory weight stages); the cost
+    # model picks the tile that fills the waves best: m=256 on 148 SMs -> 96-row tiles (240 tiles,
+    # 2 waves of the faster 96-row main loop beat 160 tiles of 128 rows)
+    for m, want in ((1, 0), (2, 0), (32, 32), (100, 128), (192, 64), (256, 96), (512, 128)):
+        p = Plan.heuristic(w, m, False, 148)
+        assert (p.bm, p.splits) == (want, 1) and p.valid_for(w, m), (m, p)
         assert Plan.heuristic(w, m, True).splits == 1 and Plan.heuristic(w, m, True).bm > 0
-    # 80 x 2 tiles of m=256 keep 148 SMs busy with whole tiles; with 400 SMs 64-row tiles (320)
-    # still cover 60 % of them; with 1000 SMs K is split (stream-K)
-    assert Plan.heuristic(w, 256, False, 148).splits == 1
+    # with 400 SMs, 64-row tiles (320) fit in one wave
     p400 = Plan.heuristic(w, 256, False, 400)
     assert (p400.bm, p400.splits) == (64, 1)
-    assert Plan.heuristic(w, 256, False, 1000).splits > 1
+    # few long tiles (N=2560, K=10240: 40 tiles of 160 k-blocks): K is split (stream-K)
+    w_long, _, _ = make_weights(gpu, KINDS["Q4_K"], 2560, 10240, seed=3)
+    assert Plan.heuristic(w_long, 256, False, 148).splits > 1
     x, x_exact = activations(32, 2560, torch.bfloat16, seed=1)
     out = torch.empty(32, 10240, device="cuda")
     matmul(gpu, Buf(x), 32, w, Buf(out), None, SplitScratch(gpu))

@@ -165,7 +165,9 @@ typedef struct jk_plan {
 #define JK_GEMV_ROWS 16 /* GEMV_ROWS (gemm.rs:1019) */
 
 /* Plan::heuristic (gemm.rs:989-1004); `sms` is the multiprocessor count to fill (the
- * reference's groups_target; 0 = the device's own count). */
+ * reference's groups_target; 0 = the device's own count). Unless row_invariant, block-quantized
+ * weights get the row tile (32/64/96/128) and schedule (whole tiles or stream-K) that a cost model
+ * of this kernel's measured main-loop rates and waves of tiles over the SMs predicts fastest. */
 jk_status jk_plan_heuristic(const jk_qmatrix *w, size_t m, int row_invariant, int sms, jk_plan *out);
 
 /* Plan::valid_for (gemm.rs:1006-1015): 1 if `plan` can run `w` at `m` rows, else 0. */

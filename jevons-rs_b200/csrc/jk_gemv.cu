@@ -48,11 +48,7 @@ constexpr int WARPS = 8;
 constexpr int THREADS = 32 * WARPS;
 constexpr int GROUP_ROWS = 8;         // weight rows per warp item (4 lanes per row)
 constexpr int SLOTS_PER_WARP = 2;
-#ifndef JK_GEMV_WARP_TARGET_OVERRIDE
 constexpr int WARP_TARGET = 1;        // K parts grow until row groups x parts >= SMs x WARPS x this
-#else
-constexpr int WARP_TARGET = JK_GEMV_WARP_TARGET_OVERRIDE;
-#endif
 constexpr int SLOT_WORDS = 40;        // per (step, lane) activation slot, 160 bytes
 // activation slot layout (words): [0,16) xq lo[32] int16 | [16,32) xq hi[32] | 32 s_lo | 33 s_hi |
 //                                 34..37 sums of xq over lo[0:16), lo[16:32), hi[0:16), hi[16:32) | pad
@@ -659,9 +655,6 @@ jk_status launch_gemv_t(const WView& w, const void* x, int x_dtype, int mrows, f
     // the SMs), but no more CTAs than row groups
     const int64_t want = (int64_t)geo.rowgroups;
     // grouped: the live jobs share the SMs
-#ifdef JK_GEMV_ONE_CTA_PER_SM
-    if (!gp.jobs && per_sm > 1) per_sm = 1;
-#endif
     const int64_t cap = ((int64_t)per_sm * sms + jobs_est - 1) / jobs_est;
     const unsigned grid = (unsigned)(want < cap ? want : cap);
     if (grid == 0) return JK_OK;

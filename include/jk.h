@@ -311,6 +311,9 @@ jk_status jk_ipc_close(int device, void *dev_ptr);
  * chunk is pushed into every peer's buffer by the copy engines (one copy stream per peer, inside
  * the library) while the next chunk's product runs, so the exchange takes no SMs from the product.
  * The copy streams carry copies only (a kernel there would wait for an SM the products hold). With
+ * 4 or more row chunks the last quarter of them is pushed to the peers by a copy kernel on `stream`
+ * once the products are done (the copy engines are still busy with the earlier chunks then, and the
+ * SMs are free). With
  * wait != 0 the call ends with jk_allgather_wait: the gathered output is complete on `stream`
  * after it. With wait == 0 the call returns with its copies still running beside `stream` (the
  * next product can overlap them): this rank's block of out_peers[rank] must then stay untouched

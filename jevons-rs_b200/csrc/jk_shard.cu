@@ -70,12 +70,25 @@ __global__ void wait_peers_kernel(uint32_t* flags, int world, int rank, uint32_t
 }
 
 // Copy streams (NSUB per peer) and events, created once per device.
+// Copy of this rank's rows [r0, r1) of its shard into every peer's gathered buffer by the SMs
+// (16-byte loads and peer stores over NVLink): grid.y = peer index (this rank skipped).
+struct PeerRows {
+    float4* d[MAX_WORLD];
+};
+__global__ void __launch_bounds__(256) push_rows_kernel(const float4* __restrict__ src, PeerRows dst, int rank,
+                                                        size_t n4) {
+    const int p = (int)blockIdx.y < rank ? (int)blockIdx.y : (int)blockIdx.y + 1;
+    float4* __restrict__ d = dst.d[p];
+    for (size_t i = (size_t)blockIdx.x * 256 + threadIdx.x; i < n4; i += (size_t)gridDim.x * 256) d[i] = src[i];
+}
+
 struct ShardState {
     bool ready = false;
     cudaStream_t cs[MAX_WORLD][NSUB] = {};
     cudaEvent_t sub[MAX_WORLD][NSUB] = {};
     cudaEvent_t chunk[MAX_CHUNKS] = {};
     cudaEvent_t done[MAX_WORLD] = {};
+    cudaEvent_t pushed = {};
 };
 
 jk_status shard_state(int device, ShardState** out) {
@@ -85,6 +98,8 @@ jk_status shard_state(int device, ShardState** out) {
     std::lock_guard<std::mutex> lock(mu);
     ShardState& s = st[device];
     if (!s.ready) {
+        if (cudaEventCreateWithFlags(&s.pushed, cudaEventDisableTiming) != cudaSuccess)
+            return cuda_fail(cudaGetLastError(), "sharded product: event set-up");
         for (int p = 0; p < MAX_WORLD; ++p) {
             cudaError_t e = cudaEventCreateWithFlags(&s.done[p], cudaEventDisableTiming);
             for (int q = 0; q < NSUB && e == cudaSuccess; ++q) {
@@ -208,6 +223,10 @@ extern "C" jk_status jk_sharded_matmul_allgather(const jk_qmatrix* w_shard, cons
     const int nchunk = (int)(units < (size_t)chunks ? units : (size_t)chunks);
     const size_t esz = jk::dtype_bytes(x_dtype);
     float* mine = out_peers[rank] + (size_t)rank * m * n_r;
+    // With 4 or more chunks the last quarter of them is pushed by the SMs once the products are
+    // done: the copy engines are still busy with the earlier chunks then, and the SMs are idle.
+    const int n_sm = world > 1 && nchunk >= 4 ? nchunk / 4 : 0;
+    size_t r_sm = m;  // first row pushed by the SMs
     for (int i = 0; i < nchunk; ++i) {
         const size_t r0 = (size_t)i * units / nchunk * unit, r1e = (size_t)(i + 1) * units / nchunk * unit;
         const size_t r1 = r1e < m ? r1e : m;
@@ -217,6 +236,10 @@ extern "C" jk_status jk_sharded_matmul_allgather(const jk_qmatrix* w_shard, cons
                        rows * n_r, scratch, stream);
         if (st != JK_OK) return st;
         if (world == 1) continue;
+        if (i >= nchunk - n_sm) {
+            if (r0 < r_sm) r_sm = r0;
+            continue;
+        }
         cudaError_t e = cudaEventRecord(ss->chunk[i], cs);
         for (int p = 0; p < world && e == cudaSuccess; ++p) {
             if (p == rank) continue;
@@ -232,6 +255,22 @@ extern "C" jk_status jk_sharded_matmul_allgather(const jk_qmatrix* w_shard, cons
         if (e != cudaSuccess) return jk::cuda_fail(e, "sharded product: chunk copies");
     }
     if (world == 1) return JK_OK;
+    if (r_sm < m) {
+        jk::PeerRows pr{};
+        for (int p = 0; p < world; ++p)
+            pr.d[p] = reinterpret_cast<float4*>(out_peers[p] + (size_t)rank * m * n_r + r_sm * n_r);
+        const size_t n4 = (m - r_sm) * n_r / 4;
+        const unsigned gx = (unsigned)jk::sm_count(w_shard->device) * 2;
+        jk::push_rows_kernel<<<dim3(gx, (unsigned)(world - 1)), 256, 0, cs>>>(
+            reinterpret_cast<const float4*>(mine + r_sm * n_r), pr, rank, n4);
+        cudaError_t e = cudaGetLastError();
+        // the peers' signals (jk_allgather_wait, on the first copy stream of each peer) follow
+        // these stores
+        if (e == cudaSuccess) e = cudaEventRecord(ss->pushed, cs);
+        for (int p = 0; p < world && e == cudaSuccess; ++p)
+            if (p != rank) e = cudaStreamWaitEvent(ss->cs[p][0], ss->pushed, 0);
+        if (e != cudaSuccess) return jk::cuda_fail(e, "sharded product: SM copies");
+    }
     if (wait) return jk_allgather_wait(w_shard->device, flags_peers, world, rank, stream);
     return JK_OK;
 }

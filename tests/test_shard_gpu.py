@@ -48,7 +48,8 @@ def _worker(rank, world, port, case, q):
         pg = PeerGather(gpu, m, hi - lo, buffers=2)
         scratch = SplitScratch(gpu)
         if case == "product":
-            for call in range(4):  # waiting per call, and two calls per wait
+            for call in range(4):  # waiting per call, two calls per wait, and SM-pushed chunks
+                buf = call % 2
                 if call < 2:
                     pg.run(w, x, i=call % 2, wait=True, chunks=3, scratch=scratch)
                 elif call == 3:
@@ -56,9 +57,15 @@ def _worker(rank, world, port, case, q):
                     pg.run(w, x, i=1, wait=False, chunks=1, scratch=scratch)
                     pg.wait()
                 else:
-                    continue
+                    # 8 chunks (7 row chunks at m=200): the last one reaches the peers through the
+                    # SMs' copy kernel; the buffer is cleared first so that stale rows cannot pass
+                    pg.output(0).zero_()
+                    torch.cuda.synchronize()
+                    dist.barrier()
+                    pg.run(w, x, i=0, wait=True, chunks=8, scratch=scratch)
+                    buf = 0
                 torch.cuda.synchronize()
-                got = pg.output(call % 2).permute(1, 0, 2).reshape(m, n_total).cpu().numpy()
+                got = pg.output(buf).permute(1, 0, 2).reshape(m, n_total).cpu().numpy()
                 dense = oracle.dequantize(oracle.Q4_K, raw).reshape(n_total, k)
                 xe = x.float().cpu().numpy()
                 want = oracle.matmul_f64(xe, dense)

@@ -202,6 +202,7 @@ struct Sched {
     const uint32_t* sorted;
     int64_t n_exp;            // weight rows (output columns) per expert
     int job_rows;             // rows per job (<= BT)
+    int64_t njobs;            // grouped: the job count jobs[0], read once per thread in the kernel
 };
 
 // Where a tile sits: its first weight row in the matrix, the first output column, its
@@ -221,7 +222,7 @@ __device__ __forceinline__ TileAt tile_at(const Sched& s, int64_t tile, int rank
         t.mend = m;
         t.live = true;
     } else {
-        t.live = mt < (int64_t)__ldg(s.jobs);
+        t.live = mt < s.njobs;
         const int64_t e = t.live ? __ldg(s.jobs + 1 + 2 * mt) : 0;
         t.m0 = t.live ? __ldg(s.jobs + 2 + 2 * mt) : 0;
         const int64_t end = t.live ? __ldg(s.offsets + e + 1) : 0;
@@ -333,8 +334,7 @@ __device__ __forceinline__ bool seg_next(const Sched& s, SegState& st, Seg& g) {
         st.next += g.kb_hi - g.kb_lo;
     } else {
         if (s.jobs) {  // grouped: every role skips the tiles of jobs past the device-side count
-            const int64_t njobs = (int64_t)__ldg(s.jobs);
-            while (st.next < st.end && st.next % s.tiles_m >= njobs) st.next += s.G;
+            while (st.next < st.end && st.next % s.tiles_m >= s.njobs) st.next += s.G;
             if (st.next >= st.end) return false;
         }
         g.tile = st.next;
@@ -696,8 +696,22 @@ __device__ __forceinline__ void dequant_role_tmem(const Sched& sched, SegState& 
     SbDequant<FMT, BF16> dq;
     int st = 0;  // stage = raw super-block counter
     Seg sg;
-    while (ok && seg_next(sched, ss, sg)) {
-        const int64_t row = tile_at<TW, BT>(sched, sg.tile, rank, 0).wrow0 + row_in_tile;
+    // Expert-grouped products look the next segment's weight row up (its expert, from the
+    // device-side job table) one segment ahead, so the table load of a tile switch overlaps this
+    // segment's decode instead of delaying the next tile's first stage. Dense products compute it.
+    bool have = seg_next(sched, ss, sg);
+    int64_t wrow0 = have && sched.jobs ? tile_at<TW, BT>(sched, sg.tile, rank, 0).wrow0 : 0;
+    while (ok && have) {
+        Seg sg_n = sg;
+        bool have_n = false;
+        int64_t wrow0_n = 0;
+        if (sched.jobs) {
+            have_n = seg_next(sched, ss, sg_n);
+            if (have_n) wrow0_n = tile_at<TW, BT>(sched, sg_n.tile, rank, 0).wrow0;
+        } else {
+            wrow0 = tile_at<TW, BT>(sched, sg.tile, rank, 0).wrow0;
+        }
+        const int64_t row = wrow0 + row_in_tile;
         const bool row_ok = row < w.rows;
         const int64_t rr = row_ok ? row : 0;
         const int sb_lo = sg.kb_lo >> 2, sb_hi = (sg.kb_hi - 1) >> 2;
@@ -742,6 +756,13 @@ __device__ __forceinline__ void dequant_role_tmem(const Sched& sched, SegState& 
                 else mbar_arrive(full(s));
                 mbar_arrive(raw_empty(slot));
             }
+        }
+        if (sched.jobs) {
+            sg = sg_n;
+            wrow0 = wrow0_n;
+            have = have_n;
+        } else {
+            have = seg_next(sched, ss, sg);
         }
     }
 }
@@ -841,7 +862,12 @@ gemm_tc_kernel(const __grid_constant__ CUtensorMap tm_x, const __grid_constant__
     // (every role), the stream-K flags and partials (epilogues, after their MMAs and so after the
     // producer) -- waits for it first; weights are read-only for the whole product.
     gdc_launch();
-    if (sched.jobs) gdc_wait();
+    if (sched.jobs) {
+        gdc_wait();
+        // the job count cannot change during the product: one load here instead of one per
+        // segment in every role (a dependent load at each tile switch)
+        sched.njobs = (int64_t)__ldg(sched.jobs);
+    }
 
     bool ok = true;
     SegState ss;
